@@ -1,0 +1,57 @@
+/*
+ * cail.h — cail-b200 public header.
+ *
+ * cail-b200 is a transparent MPI_Allreduce interposition library: load it
+ * with LD_PRELOAD, or link it before -lmpi, and every MPI_Allreduce on
+ * device buffers that it supports runs on its Blackwell NVLink kernels;
+ * everything else reaches the MPI library through PMPI_Allreduce.  No API
+ * call is needed.
+ *
+ * The functions below are optional extensions for tools and benchmarks
+ * (they are what the reference's header leaves empty, cail.h:14-18 there).
+ */
+#ifndef CAIL_H
+#define CAIL_H
+
+#include <mpi.h>
+
+#define CAIL_VERSION_MAJOR 0
+#define CAIL_VERSION_MINOR 1
+#define CAIL_VERSION_PATCH 0
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library version string, e.g. "0.1.0 (cuda sm_100a)" or "0.1.0 (host)". */
+const char *cail_version(void);
+
+/* Name of the algorithm that ran the last intercepted MPI_Allreduce of this
+ * process ("one_shot", "two_shot", "nvls", "recursive_doubling", "ring",
+ * "rabenseifner", "pmpi" for a passthrough, "none" before the first call). */
+const char *cail_last_algorithm(void);
+
+/* Counters since initialisation. */
+typedef struct cail_stats {
+    unsigned long long calls;          /* MPI_Allreduce calls seen */
+    unsigned long long passthrough;    /* calls forwarded to PMPI_Allreduce */
+    unsigned long long by_algo[8];     /* indexed by cail_algo_t + 1 (auto=0 unused) */
+    unsigned long long bytes;          /* payload bytes reduced by cail algorithms */
+    unsigned long long reg_hits;       /* registration cache hits (peer buffers) */
+    unsigned long long reg_misses;     /* registration cache misses (IPC opens) */
+    unsigned long long device_errors;  /* device collectives that reported an error */
+} cail_stats_t;
+int cail_get_stats(cail_stats_t *out);
+
+/* 1 if communicator `comm` runs cail's NVLink kernels (after its first
+ * device MPI_Allreduce), 0 if it uses the point-to-point algorithms. */
+int cail_comm_uses_nvlink(MPI_Comm comm);
+
+/* 1 if NVLS (NVSwitch multicast) is active on `comm`, else 0. */
+int cail_comm_uses_nvls(MPI_Comm comm);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAIL_H */

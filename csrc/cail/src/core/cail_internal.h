@@ -1,0 +1,96 @@
+// cail_internal.h — process-wide state, configuration and logging of cail.
+//
+// Logging keeps the reference's three levels and prefixes
+// (src/core/cail_internal.h:17-27 there): "[cail] ..." when CAIL_DEBUG is
+// on, "[cail WARN] ..." unless CAIL_WARN=0, "[cail ERROR] ..." always.  Every
+// warning goes through CAIL_WARN, including the GPU backend's (the
+// reference's CUDA backend printed its warnings unconditionally).
+#pragma once
+
+#include <mpi.h>
+#include <stddef.h>
+#include <stdio.h>
+
+#include "cail.h"
+#include "cail_types.h"
+
+#define CAIL_DBG(fmt, ...) \
+    do { if (cail_global_state.debug) fprintf(stderr, "[cail] " fmt "\n", ##__VA_ARGS__); } while (0)
+#define CAIL_ERR(fmt, ...) fprintf(stderr, "[cail ERROR] " fmt "\n", ##__VA_ARGS__)
+#define CAIL_WARN(fmt, ...) \
+    do { if (cail_global_state.warn) fprintf(stderr, "[cail WARN] " fmt "\n", ##__VA_ARGS__); } while (0)
+#define CAIL_CHECK(rc) do { if ((rc) != MPI_SUCCESS) return (rc); } while (0)
+
+// Environment variables of the reference contract.
+#define CAIL_ENV_DEBUG "CAIL_DEBUG"
+#define CAIL_ENV_ALGO "CAIL_ALGO"
+#define CAIL_ENV_MSG_SMALL_THRESHOLD "CAIL_MSG_SMALL_THRESHOLD"
+#define CAIL_ENV_NPROCS_THRESHOLD "CAIL_NPROCS_THRESHOLD"
+#define CAIL_ENV_MIN_MSG_SIZE "CAIL_MIN_MSG_SIZE"
+#define CAIL_ENV_WARN "CAIL_WARN"
+// cail-b200 additions.
+#define CAIL_ENV_DEVICE_TIMEOUT_MS "CAIL_DEVICE_TIMEOUT_MS"
+#define CAIL_ENV_NVLS "CAIL_NVLS"
+#define CAIL_ENV_ONESHOT_MAX "CAIL_ONESHOT_MAX"
+#define CAIL_ENV_TUNE_FILE "CAIL_TUNE_FILE"
+#define CAIL_ENV_STATS "CAIL_STATS"
+#define CAIL_ENV_TRACE "CAIL_TRACE"
+#define CAIL_ENV_FLUSH_RECV "CAIL_FLUSH_RECV"
+
+#define CAIL_DEFAULT_MSG_SMALL_THRESHOLD 262144U /* 256 KiB */
+#define CAIL_DEFAULT_NPROCS_THRESHOLD 4U
+#define CAIL_DEFAULT_MIN_MSG_SIZE 32768U /* 32 KiB */
+#define CAIL_DEFAULT_DEVICE_TIMEOUT_MS 10000L
+
+/* Largest power of two <= n (n > 0). */
+static inline int cail_pof2(int n) {
+    int p = 1;
+    while (p <= n / 2) p <<= 1;
+    return p;
+}
+static inline int cail_is_pof2(int n) { return n > 0 && (n & (n - 1)) == 0; }
+
+typedef struct cail_state {
+    int initialized;
+    int debug;
+    int warn;
+    size_t msg_small_threshold;
+    int msg_small_threshold_set; /* the user set CAIL_MSG_SMALL_THRESHOLD */
+    int nprocs_threshold;        /* parsed for compatibility; no dispatch rule uses it */
+    size_t min_msg_size;
+    int force_algo;
+    long device_timeout_ms;
+    int nvls;                    /* 0 off, 1 use when the fabric supports it */
+    size_t oneshot_max;          /* NVLink one-shot/two-shot crossover in bytes, 0 = tuned */
+    int flush_recv;
+    int stats;
+    FILE *trace;
+} cail_state_t;
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+extern cail_state_t cail_global_state;
+extern cail_stats_t cail_counters;
+extern int cail_last_algo;
+
+int cail_init(MPI_Comm comm);
+void cail_finalize(void);
+int cail_is_initialized(void);
+
+int cail_allreduce_dispatch(const void *sendbuf, void *recvbuf, int count, MPI_Datatype datatype,
+                            MPI_Op op, MPI_Comm comm);
+
+int cail_buf_get_tmp(void **ptr, size_t size);
+void cail_buf_release_tmp(void *ptr);
+void cail_buf_finalize(void);
+
+/* Per-call trace line (CAIL_TRACE=path): algo,bytes,count,dtype,op,nprocs,usec */
+void cail_trace_call(int algo, size_t bytes, int count, cail_datatype_t dt, cail_op_t op,
+                     int nprocs, double usec);
+double cail_now_us(void);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,904 @@
+// cail_dev_comm.cpp — per-communicator device runtime of the NVLink path.
+//
+// Setup (collective, at the first device MPI_Allreduce on a communicator):
+//   1. topology probe: PMPI_Allgather of {host id, pid, GPU UUID}; the path
+//      is used only if all ranks share a node, every rank has its own GPU,
+//      every peer GPU is visible and peer-accessible, and P <= 8;
+//   2. workspace: one cudaMalloc per rank (arrival flags + two one-shot
+//      scratch halves), exported with cudaIpcGetMemHandle, exchanged with
+//      PMPI_Allgather and opened by every peer;
+//   3. host exchange segment: POSIX shared memory with one cache-line slot
+//      per rank, used by the two-shot path to publish the IPC descriptors of
+//      the user buffers of each call and as a host barrier;
+//   4. NVLS (when every GPU reports CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED
+//      and CAIL_NVLS != 0): rank 0 creates a multicast object, passes its
+//      POSIX file descriptor to the other ranks over a Unix-domain socket
+//      (SCM_RIGHTS); each rank adds its GPU, binds its own physical memory
+//      and maps both the unicast and the multicast view.
+// Every step ends with an agreement (PMPI_Allreduce MIN of a success flag),
+// so all ranks take the same path.  The context is cached on the
+// communicator as an MPI attribute and destroyed by its delete callback.
+//
+// Registration cache: the user buffers of two-shot calls are exported once
+// per allocation (keyed by CU_POINTER_ATTRIBUTE_BUFFER_ID, which is never
+// reused) and each peer allocation is opened once (LRU of 1024 mappings).
+#include "cail_dev.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <errno.h>
+#include <fcntl.h>
+#include <sched.h>
+#include <signal.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/socket.h>
+#include <sys/stat.h>
+#include <sys/un.h>
+#include <unistd.h>
+
+#include <atomic>
+#include <list>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../core/cail_internal.h"
+#include "cail_dev_kernels.cuh"
+
+using cail::DevStatus;
+using cail::kMaxBlocks;
+using cail::kMaxRanks;
+
+namespace {
+
+// ---------------------------------------------------------------- driver API
+struct Driver {
+    bool loaded = false;
+    CUresult (*pointerGetAttribute)(void *, CUpointer_attribute, CUdeviceptr) = nullptr;
+    CUresult (*memGetAddressRange)(CUdeviceptr *, size_t *, CUdeviceptr) = nullptr;
+    CUresult (*deviceGet)(CUdevice *, int) = nullptr;
+    CUresult (*deviceGetAttribute)(int *, CUdevice_attribute, CUdevice) = nullptr;
+    CUresult (*memCreate)(CUmemGenericAllocationHandle *, size_t, const CUmemAllocationProp *,
+                          unsigned long long) = nullptr;
+    CUresult (*memRelease)(CUmemGenericAllocationHandle) = nullptr;
+    CUresult (*memAddressReserve)(CUdeviceptr *, size_t, size_t, CUdeviceptr, unsigned long long) = nullptr;
+    CUresult (*memAddressFree)(CUdeviceptr, size_t) = nullptr;
+    CUresult (*memMap)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long) = nullptr;
+    CUresult (*memUnmap)(CUdeviceptr, size_t) = nullptr;
+    CUresult (*memSetAccess)(CUdeviceptr, size_t, const CUmemAccessDesc *, size_t) = nullptr;
+    CUresult (*memGetAllocationGranularity)(size_t *, const CUmemAllocationProp *,
+                                            CUmemAllocationGranularity_flags) = nullptr;
+    CUresult (*memExportToShareableHandle)(void *, CUmemGenericAllocationHandle,
+                                           CUmemAllocationHandleType, unsigned long long) = nullptr;
+    CUresult (*memImportFromShareableHandle)(CUmemGenericAllocationHandle *, void *,
+                                             CUmemAllocationHandleType) = nullptr;
+    CUresult (*multicastCreate)(CUmemGenericAllocationHandle *, const CUmulticastObjectProp *) = nullptr;
+    CUresult (*multicastAddDevice)(CUmemGenericAllocationHandle, CUdevice) = nullptr;
+    CUresult (*multicastBindMem)(CUmemGenericAllocationHandle, size_t, CUmemGenericAllocationHandle,
+                                 size_t, size_t, unsigned long long) = nullptr;
+    CUresult (*multicastUnbind)(CUmemGenericAllocationHandle, CUdevice, size_t, size_t) = nullptr;
+    CUresult (*multicastGetGranularity)(size_t *, const CUmulticastObjectProp *,
+                                        CUmulticastGranularity_flags) = nullptr;
+};
+Driver g_drv;
+
+template <typename F>
+void load_sym(const char *name, F &fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+        fn = reinterpret_cast<F>(p);
+}
+
+void load_driver() {
+    if (g_drv.loaded) return;
+    g_drv.loaded = true;
+    load_sym("cuPointerGetAttribute", g_drv.pointerGetAttribute);
+    load_sym("cuMemGetAddressRange", g_drv.memGetAddressRange);
+    load_sym("cuDeviceGet", g_drv.deviceGet);
+    load_sym("cuDeviceGetAttribute", g_drv.deviceGetAttribute);
+    load_sym("cuMemCreate", g_drv.memCreate);
+    load_sym("cuMemRelease", g_drv.memRelease);
+    load_sym("cuMemAddressReserve", g_drv.memAddressReserve);
+    load_sym("cuMemAddressFree", g_drv.memAddressFree);
+    load_sym("cuMemMap", g_drv.memMap);
+    load_sym("cuMemUnmap", g_drv.memUnmap);
+    load_sym("cuMemSetAccess", g_drv.memSetAccess);
+    load_sym("cuMemGetAllocationGranularity", g_drv.memGetAllocationGranularity);
+    load_sym("cuMemExportToShareableHandle", g_drv.memExportToShareableHandle);
+    load_sym("cuMemImportFromShareableHandle", g_drv.memImportFromShareableHandle);
+    load_sym("cuMulticastCreate", g_drv.multicastCreate);
+    load_sym("cuMulticastAddDevice", g_drv.multicastAddDevice);
+    load_sym("cuMulticastBindMem", g_drv.multicastBindMem);
+    load_sym("cuMulticastUnbind", g_drv.multicastUnbind);
+    load_sym("cuMulticastGetGranularity", g_drv.multicastGetGranularity);
+}
+
+// ---------------------------------------------------------------- constants
+constexpr size_t kFlagBytes = 64 << 10;                 // arrival flags (16 KiB used)
+constexpr size_t kScratchHalf = 4 << 20;                // one-shot scratch per half
+constexpr size_t kWorkspaceBytes = kFlagBytes + 2 * kScratchHalf;
+constexpr size_t kNvlsCounterBytes = 2 << 20;           // counter page(s) of the multicast region
+constexpr size_t kDefaultNvlsHalf = 128ull << 20;       // NVLS staging per half
+
+// ---------------------------------------------------------------- host exchange
+struct BufDesc {
+    cudaIpcMemHandle_t handle;
+    uint64_t id;
+    uint64_t offset;
+    int32_t ok;
+    int32_t pad;
+};
+
+struct alignas(128) XSlot {
+    std::atomic<uint64_t> arrive;
+    char pad0[56];
+    std::atomic<uint64_t> depart;
+    char pad1[56];
+    BufDesc send, recv;
+    int32_t pid;
+};
+
+struct ProbeInfo {
+    unsigned long long host;
+    int pid;
+    int ordinal;
+    char uuid[16];
+    int nvls_capable;
+    int sms;
+};
+
+struct Export {
+    cudaIpcMemHandle_t handle;
+    uintptr_t base;
+    bool ok;
+};
+
+struct ImportKey {
+    int peer;
+    uint64_t id;
+    bool operator==(const ImportKey &o) const { return peer == o.peer && id == o.id; }
+};
+struct ImportKeyHash {
+    size_t operator()(const ImportKey &k) const { return std::hash<uint64_t>()(k.id * 31 + (uint64_t)k.peer); }
+};
+struct Import {
+    char *base;
+    std::list<ImportKey>::iterator lru;
+};
+constexpr size_t kMaxImports = 1024;
+
+unsigned long long host_id() {
+    char h[256] = {0};
+    gethostname(h, sizeof(h) - 1);
+    unsigned long long x = 1469598103934665603ull;
+    for (const char *p = h; *p; ++p) { x ^= (unsigned char)*p; x *= 1099511628211ull; }
+    return x;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- context
+struct cail_dev_comm {
+    MPI_Comm comm = MPI_COMM_NULL;
+    bool ok = false;
+    bool broken = false;
+    int rank = 0, P = 1, dev = -1, sms = 148;
+    cudaStream_t stream = nullptr;
+    // workspace
+    char *ws = nullptr;
+    char *peer_ws[kMaxRanks] = {};
+    uint32_t epoch = 0;
+    DevStatus *status_h = nullptr, *status_d = nullptr;
+    // host exchange
+    XSlot *xs = nullptr;
+    size_t xs_bytes = 0;
+    uint64_t xseq = 0;
+    int peer_pid[kMaxRanks] = {};
+    // registration cache
+    std::unordered_map<uint64_t, Export> exports;
+    std::unordered_map<ImportKey, Import, ImportKeyHash> imports;
+    std::list<ImportKey> lru;
+    // NVLS
+    bool nvls = false;
+    size_t nvls_half = 0, nvls_size = 0;
+    CUmemGenericAllocationHandle mc_handle = 0, phys_handle = 0;
+    CUdeviceptr uc_va = 0, mc_va = 0;
+    bool mc_bound = false;
+    uint32_t nvls_expected = 0;
+    int nvls_blocks = 0;
+    int nvls_next_half = 0;
+};
+
+namespace {
+
+int g_keyval = MPI_KEYVAL_INVALID;
+std::vector<cail_dev_comm *> g_contexts;
+int g_shm_serial = 0;
+
+void destroy_context(cail_dev_comm *dc);
+
+int delete_cb(MPI_Comm, int, void *val, void *) {
+    auto *dc = static_cast<cail_dev_comm *>(val);
+    for (auto it = g_contexts.begin(); it != g_contexts.end(); ++it)
+        if (*it == dc) { g_contexts.erase(it); break; }
+    destroy_context(dc);
+    return MPI_SUCCESS;
+}
+
+bool agree(MPI_Comm comm, bool mine) {
+    int v = mine ? 1 : 0, all = 0;
+    if (PMPI_Allreduce(&v, &all, 1, MPI_INT, MPI_MIN, comm) != MPI_SUCCESS) return false;
+    return all == 1;
+}
+
+int find_ordinal(const char uuid[16]) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return -1;
+    for (int d = 0; d < n; ++d) {
+        cudaDeviceProp p;
+        if (cudaGetDeviceProperties(&p, d) == cudaSuccess && memcmp(p.uuid.bytes, uuid, 16) == 0) return d;
+    }
+    return -1;
+}
+
+// ---- host barrier over the exchange segment
+int host_wait(cail_dev_comm *dc, bool depart, uint64_t seq) {
+    unsigned spins = 0;
+    for (int q = 0; q < dc->P; ++q) {
+        std::atomic<uint64_t> &a = depart ? dc->xs[q].depart : dc->xs[q].arrive;
+        while (a.load(std::memory_order_acquire) < seq) {
+            if (++spins % 4096 == 0) {
+                if (dc->peer_pid[q] > 0 && kill(dc->peer_pid[q], 0) != 0 && errno == ESRCH) {
+                    CAIL_ERR("rank %d: peer rank %d (pid %d) is gone", dc->rank, q, dc->peer_pid[q]);
+                    return MPI_ERR_OTHER;
+                }
+                if (spins > (1u << 20)) sched_yield();
+            }
+        }
+    }
+    return MPI_SUCCESS;
+}
+
+// ---- registration cache
+bool describe(cail_dev_comm *dc, const void *p, BufDesc *d) {
+    memset(d, 0, sizeof(*d));
+    if (!g_drv.pointerGetAttribute || !g_drv.memGetAddressRange) return false;
+    unsigned long long id = 0;
+    if (g_drv.pointerGetAttribute(&id, CU_POINTER_ATTRIBUTE_BUFFER_ID, (CUdeviceptr)p) != CUDA_SUCCESS)
+        return false;
+    auto it = dc->exports.find(id);
+    if (it == dc->exports.end()) {
+        Export ex{};
+        CUdeviceptr base = 0;
+        size_t size = 0;
+        ex.ok = g_drv.memGetAddressRange(&base, &size, (CUdeviceptr)p) == CUDA_SUCCESS &&
+                cudaIpcGetMemHandle(&ex.handle, (void *)base) == cudaSuccess;
+        if (!ex.ok) cudaGetLastError();
+        ex.base = (uintptr_t)base;
+        it = dc->exports.emplace(id, ex).first;
+    }
+    if (!it->second.ok) return false;
+    d->handle = it->second.handle;
+    d->id = id;
+    d->offset = (uint64_t)((uintptr_t)p - it->second.base);
+    d->ok = 1;
+    return true;
+}
+
+char *import_buf(cail_dev_comm *dc, int q, const BufDesc &d) {
+    ImportKey k{q, d.id};
+    auto it = dc->imports.find(k);
+    if (it != dc->imports.end()) {
+        dc->lru.splice(dc->lru.begin(), dc->lru, it->second.lru);
+        cail_counters.reg_hits++;
+        return it->second.base + d.offset;
+    }
+    void *base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, d.handle, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        CAIL_ERR("rank %d: cannot open rank %d's buffer: %s", dc->rank, q, cudaGetErrorString(e));
+        cudaGetLastError();
+        return nullptr;
+    }
+    cail_counters.reg_misses++;
+    if (dc->imports.size() >= kMaxImports) {
+        ImportKey old = dc->lru.back();
+        dc->lru.pop_back();
+        auto o = dc->imports.find(old);
+        if (o != dc->imports.end()) {
+            cudaIpcCloseMemHandle(o->second.base);
+            dc->imports.erase(o);
+        }
+    }
+    dc->lru.push_front(k);
+    dc->imports[k] = Import{(char *)base, dc->lru.begin()};
+    return (char *)base + d.offset;
+}
+
+// ---- Unix-socket file descriptor passing (NVLS handle exchange)
+bool send_fd(int sock, int fd) {
+    char byte = 0;
+    struct iovec iov = {&byte, 1};
+    char ctrl[CMSG_SPACE(sizeof(int))];
+    memset(ctrl, 0, sizeof(ctrl));
+    struct msghdr m;
+    memset(&m, 0, sizeof(m));
+    m.msg_iov = &iov;
+    m.msg_iovlen = 1;
+    m.msg_control = ctrl;
+    m.msg_controllen = sizeof(ctrl);
+    struct cmsghdr *c = CMSG_FIRSTHDR(&m);
+    c->cmsg_level = SOL_SOCKET;
+    c->cmsg_type = SCM_RIGHTS;
+    c->cmsg_len = CMSG_LEN(sizeof(int));
+    memcpy(CMSG_DATA(c), &fd, sizeof(int));
+    return sendmsg(sock, &m, 0) == 1;
+}
+
+int recv_fd(int sock) {
+    char byte;
+    struct iovec iov = {&byte, 1};
+    char ctrl[CMSG_SPACE(sizeof(int))];
+    struct msghdr m;
+    memset(&m, 0, sizeof(m));
+    m.msg_iov = &iov;
+    m.msg_iovlen = 1;
+    m.msg_control = ctrl;
+    m.msg_controllen = sizeof(ctrl);
+    if (recvmsg(sock, &m, 0) != 1) return -1;
+    struct cmsghdr *c = CMSG_FIRSTHDR(&m);
+    if (!c || c->cmsg_type != SCM_RIGHTS) return -1;
+    int fd;
+    memcpy(&fd, CMSG_DATA(c), sizeof(int));
+    return fd;
+}
+
+// Shares rank 0's file descriptor with every rank.  Returns the local fd
+// (rank 0: its own) or -1.  Collective.
+int share_fd(cail_dev_comm *dc, int fd0) {
+    char name[108] = {0};
+    int lsock = -1;
+    if (dc->rank == 0) {
+        snprintf(name + 1, sizeof(name) - 2, "cail-nvls-%d-%d", (int)getpid(), ++g_shm_serial);
+        lsock = socket(AF_UNIX, SOCK_STREAM, 0);
+        struct sockaddr_un a;
+        memset(&a, 0, sizeof(a));
+        a.sun_family = AF_UNIX;
+        memcpy(a.sun_path, name, sizeof(a.sun_path));
+        socklen_t len = (socklen_t)(offsetof(struct sockaddr_un, sun_path) + 1 + strlen(name + 1));
+        if (lsock < 0 || bind(lsock, (struct sockaddr *)&a, len) != 0 || listen(lsock, 64) != 0) {
+            if (lsock >= 0) close(lsock);
+            lsock = -1;
+            name[1] = 0;
+        }
+    }
+    PMPI_Bcast(name, sizeof(name), MPI_CHAR, 0, dc->comm);
+    if (name[1] == 0) return -1;
+    int fd = -1;
+    if (dc->rank == 0) {
+        bool ok = true;
+        for (int i = 1; i < dc->P; ++i) {
+            int c = accept(lsock, nullptr, nullptr);
+            if (c < 0 || !send_fd(c, fd0)) ok = false;
+            if (c >= 0) close(c);
+        }
+        close(lsock);
+        fd = ok ? fd0 : -1;
+    } else {
+        int s = socket(AF_UNIX, SOCK_STREAM, 0);
+        struct sockaddr_un a;
+        memset(&a, 0, sizeof(a));
+        a.sun_family = AF_UNIX;
+        memcpy(a.sun_path, name, sizeof(a.sun_path));
+        socklen_t len = (socklen_t)(offsetof(struct sockaddr_un, sun_path) + 1 + strlen(name + 1));
+        if (s >= 0 && connect(s, (struct sockaddr *)&a, len) == 0) fd = recv_fd(s);
+        if (s >= 0) close(s);
+    }
+    return fd;
+}
+
+void nvls_teardown(cail_dev_comm *dc) {
+    if (dc->mc_va) {
+        g_drv.memUnmap(dc->mc_va, dc->nvls_size);
+        g_drv.memAddressFree(dc->mc_va, dc->nvls_size);
+        dc->mc_va = 0;
+    }
+    if (dc->mc_bound) {
+        CUdevice cd;
+        g_drv.deviceGet(&cd, dc->dev);
+        g_drv.multicastUnbind(dc->mc_handle, cd, 0, dc->nvls_size);
+        dc->mc_bound = false;
+    }
+    if (dc->uc_va) {
+        g_drv.memUnmap(dc->uc_va, dc->nvls_size);
+        g_drv.memAddressFree(dc->uc_va, dc->nvls_size);
+        dc->uc_va = 0;
+    }
+    if (dc->phys_handle) { g_drv.memRelease(dc->phys_handle); dc->phys_handle = 0; }
+    if (dc->mc_handle) { g_drv.memRelease(dc->mc_handle); dc->mc_handle = 0; }
+    dc->nvls = false;
+}
+
+// Collective NVLS setup.  Leaves dc->nvls false (on every rank) on failure.
+void nvls_setup(cail_dev_comm *dc, bool all_capable) {
+    if (!all_capable || !cail_global_state.nvls || dc->P < 2) return;
+    if (!g_drv.multicastCreate || !g_drv.multicastBindMem || !g_drv.memCreate) return;
+    size_t half = kDefaultNvlsHalf;
+    if (const char *e = getenv("CAIL_NVLS_CHUNK")) {
+        long v = atol(e);
+        if (v >= (1 << 20)) half = (size_t)v;
+    }
+    CUdevice cd;
+    bool ok = g_drv.deviceGet(&cd, dc->dev) == CUDA_SUCCESS;
+    CUmulticastObjectProp mp;
+    memset(&mp, 0, sizeof(mp));
+    mp.numDevices = (unsigned)dc->P;
+    mp.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+    CUmemAllocationProp ap;
+    memset(&ap, 0, sizeof(ap));
+    ap.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+    ap.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    ap.location.id = cd;
+    size_t g1 = 0, g2 = 0;
+    mp.size = kNvlsCounterBytes + 2 * half;
+    ok = ok && g_drv.multicastGetGranularity(&g1, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED) == CUDA_SUCCESS;
+    ok = ok && g_drv.memGetAllocationGranularity(&g2, &ap, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED) == CUDA_SUCCESS;
+    size_t gran = g1 > g2 ? g1 : g2;
+    if (gran == 0) gran = 2 << 20;
+    size_t size = (kNvlsCounterBytes + 2 * half + gran - 1) / gran * gran;
+    mp.size = size;
+    dc->nvls_size = size;
+    dc->nvls_half = half;
+    if (!agree(dc->comm, ok)) return;
+
+    int fd = -1;
+    if (dc->rank == 0) {
+        ok = g_drv.multicastCreate(&dc->mc_handle, &mp) == CUDA_SUCCESS &&
+             g_drv.memExportToShareableHandle(&fd, dc->mc_handle, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0) == CUDA_SUCCESS;
+    }
+    if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }
+    int myfd = share_fd(dc, fd);
+    ok = myfd >= 0;
+    if (ok && dc->rank != 0)
+        ok = g_drv.memImportFromShareableHandle(&dc->mc_handle, (void *)(uintptr_t)myfd,
+                                                CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR) == CUDA_SUCCESS;
+    if (myfd >= 0) close(myfd);
+    if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }
+    ok = g_drv.multicastAddDevice(dc->mc_handle, cd) == CUDA_SUCCESS;
+    if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }  // every device added before binding
+    ok = g_drv.memCreate(&dc->phys_handle, size, &ap, 0) == CUDA_SUCCESS;
+    ok = ok && g_drv.multicastBindMem(dc->mc_handle, 0, dc->phys_handle, 0, size, 0) == CUDA_SUCCESS;
+    dc->mc_bound = ok;
+    CUmemAccessDesc acc;
+    memset(&acc, 0, sizeof(acc));
+    acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    acc.location.id = cd;
+    acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+    ok = ok && g_drv.memAddressReserve(&dc->uc_va, size, gran, 0, 0) == CUDA_SUCCESS;
+    ok = ok && g_drv.memMap(dc->uc_va, size, 0, dc->phys_handle, 0) == CUDA_SUCCESS;
+    ok = ok && g_drv.memSetAccess(dc->uc_va, size, &acc, 1) == CUDA_SUCCESS;
+    ok = ok && g_drv.memAddressReserve(&dc->mc_va, size, gran, 0, 0) == CUDA_SUCCESS;
+    ok = ok && g_drv.memMap(dc->mc_va, size, 0, dc->mc_handle, 0) == CUDA_SUCCESS;
+    ok = ok && g_drv.memSetAccess(dc->mc_va, size, &acc, 1) == CUDA_SUCCESS;
+    ok = ok && cudaMemset((void *)dc->uc_va, 0, kNvlsCounterBytes) == cudaSuccess &&
+         cudaDeviceSynchronize() == cudaSuccess;
+    if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }
+    // two 512-thread CTAs per SM are always co-resident, which the
+    // grid-wide counter barrier of the NVLS kernel requires
+    dc->nvls_blocks = dc->sms * 2;
+    dc->nvls = true;
+    CAIL_DBG("nvls: multicast region of %zu bytes, staging 2 x %zu", size, half);
+}
+
+void destroy_context(cail_dev_comm *dc) {
+    if (!dc) return;
+    if (dc->ok) {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        if (dc->dev >= 0) cudaSetDevice(dc->dev);
+        if (dc->stream) cudaStreamSynchronize(dc->stream);
+        nvls_teardown(dc);
+        for (auto &kv : dc->imports) cudaIpcCloseMemHandle(kv.second.base);
+        dc->imports.clear();
+        for (int q = 0; q < dc->P; ++q)
+            if (q != dc->rank && dc->peer_ws[q]) cudaIpcCloseMemHandle(dc->peer_ws[q]);
+        if (dc->ws) cudaFree(dc->ws);
+        if (dc->status_h) cudaFreeHost(dc->status_h);
+        if (dc->stream) cudaStreamDestroy(dc->stream);
+        if (dc->xs) munmap(dc->xs, dc->xs_bytes);
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+    delete dc;
+}
+
+cail_dev_comm *create_context(MPI_Comm comm) {
+    auto *dc = new cail_dev_comm();
+    dc->comm = comm;
+    PMPI_Comm_rank(comm, &dc->rank);
+    PMPI_Comm_size(comm, &dc->P);
+    load_driver();
+    cudaGetDevice(&dc->dev);
+    cudaFree(0);  // make the device's primary context current for driver calls
+
+    // 1. topology probe
+    ProbeInfo me;
+    memset(&me, 0, sizeof(me));
+    me.host = host_id();
+    me.pid = (int)getpid();
+    me.ordinal = dc->dev;
+    cudaDeviceProp prop;
+    bool ok = cudaGetDeviceProperties(&prop, dc->dev) == cudaSuccess;
+    if (ok) {
+        memcpy(me.uuid, prop.uuid.bytes, 16);
+        me.sms = prop.multiProcessorCount;
+    }
+    int mc = 0;
+    CUdevice cd;
+    if (g_drv.deviceGet && g_drv.deviceGetAttribute && g_drv.deviceGet(&cd, dc->dev) == CUDA_SUCCESS)
+        g_drv.deviceGetAttribute(&mc, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, cd);
+    me.nvls_capable = mc;
+    std::vector<ProbeInfo> all(dc->P);
+    if (PMPI_Allgather(&me, sizeof(me), MPI_BYTE, all.data(), sizeof(me), MPI_BYTE, comm) != MPI_SUCCESS)
+        ok = false;
+    bool all_nvls = true;
+    ok = ok && dc->P <= kMaxRanks;
+    for (int q = 0; ok && q < dc->P; ++q) {
+        dc->peer_pid[q] = all[q].pid;
+        if (all[q].host != me.host) ok = false;
+        if (!all[q].nvls_capable) all_nvls = false;
+        for (int r = 0; r < q; ++r)
+            if (memcmp(all[q].uuid, all[r].uuid, 16) == 0) ok = false;  // shared GPU
+        if (q == dc->rank) continue;
+        int o = find_ordinal(all[q].uuid), can = 0;
+        if (o < 0 || cudaDeviceCanAccessPeer(&can, dc->dev, o) != cudaSuccess || !can) ok = false;
+    }
+    dc->sms = me.sms > 0 ? me.sms : 148;
+    if (!agree(comm, ok)) {
+        CAIL_DBG("nvlink path unavailable on this communicator (probe)");
+        return dc;  // ok == false
+    }
+
+    // 2. workspace
+    ok = cudaStreamCreateWithFlags(&dc->stream, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaMalloc(&dc->ws, kWorkspaceBytes) == cudaSuccess;
+    ok = ok && cudaMemset(dc->ws, 0, kFlagBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+    ok = ok && cudaHostAlloc((void **)&dc->status_h, sizeof(DevStatus), cudaHostAllocMapped) == cudaSuccess;
+    ok = ok && cudaHostGetDevicePointer((void **)&dc->status_d, dc->status_h, 0) == cudaSuccess;
+    if (ok) memset(dc->status_h, 0, sizeof(DevStatus));
+    cudaIpcMemHandle_t h;
+    memset(&h, 0, sizeof(h));
+    ok = ok && cudaIpcGetMemHandle(&h, dc->ws) == cudaSuccess;
+    std::vector<cudaIpcMemHandle_t> hs(dc->P);
+    int ag = PMPI_Allgather(&h, sizeof(h), MPI_BYTE, hs.data(), sizeof(h), MPI_BYTE, comm);
+    ok = ok && ag == MPI_SUCCESS;
+    for (int q = 0; ok && q < dc->P; ++q) {
+        if (q == dc->rank) { dc->peer_ws[q] = dc->ws; continue; }
+        void *p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, hs[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) ok = false;
+        dc->peer_ws[q] = (char *)p;
+    }
+    if (!ok) cudaGetLastError();
+
+    // 3. host exchange segment
+    char name[64] = {0};
+    dc->xs_bytes = sizeof(XSlot) * kMaxRanks;
+    if (dc->rank == 0) {
+        snprintf(name, sizeof(name), "/cail_x%d_%d", (int)getpid(), ++g_shm_serial);
+        shm_unlink(name);
+        int fd = shm_open(name, O_CREAT | O_EXCL | O_RDWR, 0600);
+        if (fd < 0 || ftruncate(fd, (off_t)dc->xs_bytes) != 0) name[0] = 0;
+        if (fd >= 0) close(fd);
+    }
+    PMPI_Bcast(name, sizeof(name), MPI_CHAR, 0, comm);
+    if (name[0]) {
+        int fd = shm_open(name, O_RDWR, 0600);
+        void *m = fd >= 0 ? mmap(nullptr, dc->xs_bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0) : MAP_FAILED;
+        if (fd >= 0) close(fd);
+        if (m == MAP_FAILED) ok = false;
+        else dc->xs = (XSlot *)m;
+    } else {
+        ok = false;
+    }
+    PMPI_Barrier(comm);
+    if (dc->rank == 0 && name[0]) shm_unlink(name);
+    if (dc->xs) dc->xs[dc->rank].pid = (int32_t)getpid();
+    dc->ok = agree(comm, ok);
+    if (!dc->ok) {
+        CAIL_DBG("nvlink path unavailable on this communicator (workspace setup)");
+        dc->ok = true;  // let destroy_context release what was created
+        destroy_context(dc);
+        dc = new cail_dev_comm();
+        dc->comm = comm;
+        return dc;
+    }
+
+    // 4. NVLS
+    nvls_setup(dc, all_nvls);
+    CAIL_DBG("nvlink path: P=%d device=%d sms=%d nvls=%d", dc->P, dc->dev, dc->sms, (int)dc->nvls);
+    return dc;
+}
+
+int check_status(cail_dev_comm *dc, const char *what) {
+    cudaError_t e = cudaStreamSynchronize(dc->stream);
+    if (e != cudaSuccess) {
+        CAIL_ERR("%s: CUDA error %s", what, cudaGetErrorString(e));
+        dc->broken = true;
+        return MPI_ERR_OTHER;
+    }
+    if (dc->status_h->code != 0) {
+        const DevStatus &s = *dc->status_h;
+        CAIL_ERR("%s: rank %d gave up after %ld ms waiting for %s %d (block %d, epoch %u, saw %u)",
+                 what, s.rank, cail_global_state.device_timeout_ms,
+                 s.waited_on >= 0 ? "rank" : "barrier", s.waited_on >= 0 ? s.waited_on : -1 - s.waited_on,
+                 s.block, s.epoch, s.seen);
+        memset(dc->status_h, 0, sizeof(DevStatus));
+        dc->broken = true;
+        return MPI_ERR_OTHER;
+    }
+    return MPI_SUCCESS;
+}
+
+unsigned long long timeout_ns() { return (unsigned long long)cail_global_state.device_timeout_ms * 1000000ull; }
+
+// ---- one-shot
+int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec,
+                bool sync) {
+    const size_t bytes = count * esz;
+    cail::OneShotArgs a;
+    memset(&a, 0, sizeof(a));
+    a.src = src;
+    a.dst = dst;
+    a.count = count;
+    a.P = dc->P;
+    a.rank = dc->rank;
+    a.epoch = ++dc->epoch;
+    const size_t half = (a.epoch & 1) ? kScratchHalf : 0;
+    for (int q = 0; q < dc->P; ++q) {
+        a.scratch[q] = dc->peer_ws[q] + kFlagBytes + half;
+        a.peer_flags[q] = (uint32_t *)dc->peer_ws[q];
+    }
+    a.my_scratch = dc->ws + kFlagBytes + half;
+    a.my_flags = (uint32_t *)dc->ws;
+    a.timeout_ns = timeout_ns();
+    a.status = dc->status_d;
+    // ~2 vectors per thread, 512 threads per block
+    size_t vec = (bytes + 15) / 16;
+    int threads = 512;
+    size_t want = (vec + 2 * threads - 1) / (2 * threads);
+    int blocks = (int)(want < 1 ? 1 : (want > (size_t)kMaxBlocks ? kMaxBlocks : want));
+    if (const char *e = getenv("CAIL_ONESHOT_BLOCKS")) {
+        int b = atoi(e);
+        if (b >= 1 && b <= kMaxBlocks) blocks = b;
+    }
+    cudaError_t e = cail::launch_oneshot(op, ec, a, blocks, threads, dc->stream);
+    if (e != cudaSuccess) {
+        CAIL_ERR("one_shot launch failed: %s", cudaGetErrorString(e));
+        return MPI_ERR_OTHER;
+    }
+    return sync ? check_status(dc, "one_shot") : MPI_SUCCESS;
+}
+
+int run_oneshot_chunked(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz,
+                        int op, int ec) {
+    size_t per = kScratchHalf / esz;
+    for (size_t off = 0; off < count; off += per) {
+        size_t n = count - off < per ? count - off : per;
+        int rc = run_oneshot(dc, src + off * esz, dst + off * esz, n, esz, op, ec, false);
+        if (rc != MPI_SUCCESS) return rc;
+    }
+    return check_status(dc, "one_shot");
+}
+
+// ---- two-shot over registered user buffers
+int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec) {
+    XSlot &me = dc->xs[dc->rank];
+    describe(dc, src, &me.send);
+    describe(dc, dst, &me.recv);
+    uint64_t seq = ++dc->xseq;
+    me.arrive.store(seq, std::memory_order_release);
+    int rc = host_wait(dc, false, seq);
+    if (rc != MPI_SUCCESS) return rc;
+    bool all_ok = true;
+    for (int q = 0; q < dc->P; ++q) all_ok = all_ok && dc->xs[q].send.ok && dc->xs[q].recv.ok;
+    if (!all_ok) {
+        // some rank's buffer cannot be exported: every rank sees the same
+        // descriptors and takes the copy-in path instead
+        rc = run_oneshot_chunked(dc, src, dst, count, esz, op, ec);
+    } else {
+        cail::TwoShotArgs a;
+        memset(&a, 0, sizeof(a));
+        a.P = dc->P;
+        a.rank = dc->rank;
+        a.count = count;
+        bool bad = false;
+        for (int q = 0; q < dc->P; ++q) {
+            if (q == dc->rank) {
+                a.src[q] = src;
+                a.dst[q] = dst;
+                continue;
+            }
+            a.src[q] = import_buf(dc, q, dc->xs[q].send);
+            a.dst[q] = import_buf(dc, q, dc->xs[q].recv);
+            if (!a.src[q] || !a.dst[q]) bad = true;
+        }
+        if (bad) {
+            dc->broken = true;
+            return MPI_ERR_OTHER;
+        }
+        uint64_t mis = (uint64_t)(uintptr_t)src & 15;
+        bool vec_ok = true;
+        for (int q = 0; q < dc->P; ++q)
+            if (((uintptr_t)a.src[q] & 15) != mis || ((uintptr_t)a.dst[q] & 15) != mis) vec_ok = false;
+        a.vector_ok = vec_ok ? 1 : 0;
+        if (vec_ok) {
+            size_t head = ((16 - mis) & 15) / esz;
+            if (head > count) head = count;
+            a.head = head;
+            a.nvec = (count - head) * esz / 16;
+        }
+        size_t work = vec_ok ? a.nvec / dc->P + 1 : count / dc->P + 1;
+        int threads = 512;
+        size_t want = (work + threads - 1) / threads;
+        int maxb = dc->sms * 2;
+        int blocks = (int)(want < 1 ? 1 : (want > (size_t)maxb ? maxb : want));
+        cudaError_t e = cail::launch_twoshot(op, ec, a, blocks, threads, dc->stream);
+        if (e != cudaSuccess) {
+            CAIL_ERR("two_shot launch failed: %s", cudaGetErrorString(e));
+            rc = MPI_ERR_OTHER;
+        } else {
+            rc = check_status(dc, "two_shot");
+        }
+    }
+    // depart: peers may only return (and reuse their buffers) once every
+    // rank's kernel has finished reading and writing them
+    me.depart.store(seq, std::memory_order_release);
+    int rc2 = host_wait(dc, true, seq);
+    return rc != MPI_SUCCESS ? rc : rc2;
+}
+
+// ---- NVLS
+int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec) {
+    const size_t per = dc->nvls_half / esz;
+    char *uc = (char *)dc->uc_va + kNvlsCounterBytes;
+    char *mcp = (char *)dc->mc_va + kNvlsCounterBytes;
+    const int blocks = dc->nvls_blocks;
+    const uint32_t step = (uint32_t)(dc->P * blocks);
+    for (size_t off = 0; off < count; off += per) {
+        size_t n = count - off < per ? count - off : per;
+        int h = dc->nvls_next_half;
+        dc->nvls_next_half ^= 1;
+        cail::NvlsArgs a;
+        memset(&a, 0, sizeof(a));
+        a.src = src + off * esz;
+        a.dst = dst + off * esz;
+        a.uc = uc + (size_t)h * dc->nvls_half;
+        a.mc = mcp + (size_t)h * dc->nvls_half;
+        a.mc_counter = (uint32_t *)dc->mc_va;
+        a.uc_counter = (const uint32_t *)dc->uc_va;
+        a.count = n;
+        a.P = dc->P;
+        a.rank = dc->rank;
+        dc->nvls_expected += step;
+        a.target_a = dc->nvls_expected;
+        dc->nvls_expected += step;
+        a.target_b = dc->nvls_expected;
+        a.timeout_ns = timeout_ns();
+        a.status = dc->status_d;
+        cudaError_t e = cail::launch_nvls(op, ec, a, blocks, 512, dc->stream);
+        if (e != cudaSuccess) {
+            CAIL_ERR("nvls launch failed: %s", cudaGetErrorString(e));
+            dc->broken = true;
+            return MPI_ERR_OTHER;
+        }
+    }
+    return check_status(dc, "nvls");
+}
+
+size_t default_oneshot_max(int P) {
+    // measured crossovers are loaded from CAIL_TUNE_FILE when given
+    (void)P;
+    return 512 << 10;
+}
+
+size_t nvls_min_bytes() {
+    if (const char *e = getenv("CAIL_NVLS_MIN")) return (size_t)atoll(e);
+    return 4 << 20;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- public
+extern "C" {
+
+cail_dev_comm *cail_dev_comm_get(MPI_Comm comm) {
+    if (g_keyval == MPI_KEYVAL_INVALID &&
+        PMPI_Comm_create_keyval(MPI_COMM_NULL_COPY_FN, delete_cb, &g_keyval, nullptr) != MPI_SUCCESS)
+        return nullptr;
+    void *val = nullptr;
+    int flag = 0;
+    PMPI_Comm_get_attr(comm, g_keyval, &val, &flag);
+    cail_dev_comm *dc = flag ? static_cast<cail_dev_comm *>(val) : nullptr;
+    if (!dc) {
+        dc = create_context(comm);
+        g_contexts.push_back(dc);
+        PMPI_Comm_set_attr(comm, g_keyval, dc);
+    }
+    return dc->ok ? dc : nullptr;
+}
+
+int cail_dev_nvls_ok(cail_dev_comm *dc, cail_datatype_t dt, cail_op_t op) {
+    if (!dc || !dc->nvls) return 0;
+    return cail::nvls_supported((int)op, (int)cail_elem_class(dt));
+}
+
+int cail_dev_pick_algo(cail_dev_comm *dc, size_t bytes, int count, cail_datatype_t dt, cail_op_t op) {
+    (void)count;
+    const cail_state_t &s = cail_global_state;
+    size_t one_max = s.oneshot_max ? s.oneshot_max
+                                   : (s.msg_small_threshold_set ? s.msg_small_threshold - 1
+                                                                : default_oneshot_max(dc->P));
+    if (dc->P == 1 || bytes <= one_max) return CAIL_ALGO_ONE_SHOT;
+    if (cail_dev_nvls_ok(dc, dt, op) && bytes >= nvls_min_bytes()) return CAIL_ALGO_NVLS;
+    return CAIL_ALGO_TWO_SHOT;
+}
+
+int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *recvbuf, int count,
+                       cail_datatype_t dt, cail_op_t op) {
+    if (dc->broken) {
+        CAIL_ERR("nvlink context of this communicator failed earlier; refusing further calls");
+        return MPI_ERR_OTHER;
+    }
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != dc->dev) cudaSetDevice(dc->dev);
+    const size_t esz = (size_t)cail_type_size(dt);
+    const char *src = (const char *)(sendbuf == MPI_IN_PLACE ? recvbuf : sendbuf);
+    char *dst = (char *)recvbuf;
+    const int ec = (int)cail_elem_class(dt);
+    int rc = MPI_SUCCESS;
+    if (dc->P == 1) {
+        if (src != dst && cudaMemcpyAsync(dst, src, (size_t)count * esz, cudaMemcpyDefault, dc->stream) != cudaSuccess)
+            rc = MPI_ERR_OTHER;
+        if (rc == MPI_SUCCESS) rc = check_status(dc, "copy");
+    } else if (algo == CAIL_ALGO_ONE_SHOT) {
+        rc = run_oneshot_chunked(dc, src, dst, (size_t)count, esz, (int)op, ec);
+    } else if (algo == CAIL_ALGO_NVLS && cail_dev_nvls_ok(dc, dt, op)) {
+        rc = run_nvls(dc, src, dst, (size_t)count, esz, (int)op, ec);
+    } else {
+        rc = run_twoshot(dc, src, dst, (size_t)count, esz, (int)op, ec);
+    }
+    if (prev >= 0 && prev != dc->dev) cudaSetDevice(prev);
+    return rc;
+}
+
+void cail_dev_finalize_all(void) {
+    // Deleting the attribute runs delete_cb, which destroys the context.
+    std::vector<cail_dev_comm *> all = g_contexts;
+    for (cail_dev_comm *dc : all) {
+        if (dc->ok) PMPI_Barrier(dc->comm);
+        PMPI_Comm_delete_attr(dc->comm, g_keyval);
+    }
+    g_contexts.clear();
+    if (g_keyval != MPI_KEYVAL_INVALID) PMPI_Comm_free_keyval(&g_keyval);
+}
+
+int cail_comm_uses_nvlink(MPI_Comm comm) {
+    if (g_keyval == MPI_KEYVAL_INVALID) return 0;
+    void *val = nullptr;
+    int flag = 0;
+    PMPI_Comm_get_attr(comm, g_keyval, &val, &flag);
+    return flag && val && static_cast<cail_dev_comm *>(val)->ok ? 1 : 0;
+}
+
+int cail_comm_uses_nvls(MPI_Comm comm) {
+    if (g_keyval == MPI_KEYVAL_INVALID) return 0;
+    void *val = nullptr;
+    int flag = 0;
+    PMPI_Comm_get_attr(comm, g_keyval, &val, &flag);
+    return flag && val && static_cast<cail_dev_comm *>(val)->nvls ? 1 : 0;
+}
+
+}  // extern "C"

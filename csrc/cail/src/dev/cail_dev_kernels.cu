@@ -1,0 +1,443 @@
+// cail_dev_kernels.cu — sm_100a kernels of the NVLink allreduce.
+//
+// These replace the reference's host-driven exchange + separate reduce
+// kernel (src/gpu/cuda/cail_cuda_reduce.cu:44-136 there, launched once per
+// PMPI_Sendrecv step): one launch moves the data over NVLink 5 by loading and
+// storing peer GPUs' memory directly and applies the MPI operator on the fly.
+// The reduction is a bandwidth-bound stream, so the kernels use 16-byte
+// vector loads/stores on plain SIMT threads; tensor cores and TMA have no
+// role here, and no TMA multicast load exists anywhere in this file.
+//
+// Cross-GPU synchronisation uses 32-bit epoch flags written with
+// st.release.sys into the peer's flag array and polled with ld.acquire.sys;
+// epochs only grow, so flags never need resetting.  Every poll is bounded by
+// %globaltimer: after timeout_ns the kernel records DevStatus and returns,
+// leaving the context usable.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../gpu/cail_ops.h"
+#include "cail_dev_kernels.cuh"
+
+namespace cail {
+
+namespace {
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// 16-byte vector load of (possibly peer) memory, bypassing L1.
+__device__ __forceinline__ uint4 ld_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_v4(void *p, uint4 v) {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+template <int OP, typename T>
+__device__ __forceinline__ uint4 vop(uint4 a, uint4 b) {
+    T *pa = reinterpret_cast<T *>(&a);
+    const T *pb = reinterpret_cast<const T *>(&b);
+#pragma unroll
+    for (int i = 0; i < (int)(16 / sizeof(T)); ++i) pa[i] = apply<OP, T>(pa[i], pb[i]);
+    return a;
+}
+
+// Waits until flag >= epoch (wrap-safe).  Returns false on timeout.
+__device__ __forceinline__ bool wait_flag(const uint32_t *flag, uint32_t epoch,
+                                          unsigned long long deadline, uint32_t *seen) {
+    uint32_t v = ld_acquire_sys(flag);
+    while ((int32_t)(v - epoch) < 0) {
+        if (globaltimer() > deadline) {
+            *seen = v;
+            return false;
+        }
+        v = ld_acquire_sys(flag);
+    }
+    return true;
+}
+
+__device__ void report(DevStatus *st, int rank, int peer, int block, uint32_t epoch, uint32_t seen) {
+    if (atomicCAS(&st->code, 0, 1) == 0) {
+        st->rank = rank;
+        st->waited_on = peer;
+        st->block = block;
+        st->epoch = epoch;
+        st->seen = seen;
+        __threadfence_system();
+    }
+}
+
+// Copies bytes [0, n) from src to dst (dst 16-byte aligned); src may be
+// unaligned, in which case the copy goes element by element.
+template <typename T>
+__device__ __forceinline__ void block_copy(char *dst, const char *src, size_t n) {
+    if (((uintptr_t)src & 15) == 0) {
+        size_t nv = n / 16;
+        for (size_t i = threadIdx.x; i < nv; i += blockDim.x)
+            st_v4(dst + i * 16, *reinterpret_cast<const uint4 *>(src + i * 16));
+        for (size_t e = nv * 16 / sizeof(T) + threadIdx.x; e < n / sizeof(T); e += blockDim.x)
+            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+    } else {
+        for (size_t e = threadIdx.x; e < n / sizeof(T); e += blockDim.x)
+            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+    }
+}
+
+// ---------------------------------------------------------------- one-shot
+template <int OP, typename T>
+__global__ void __launch_bounds__(512) oneshot_kernel(OneShotArgs a) {
+    __shared__ int s_fail;
+    const size_t bytes = a.count * sizeof(T);
+    const size_t n16 = (bytes + 15) / 16;
+    const size_t per = (n16 + gridDim.x - 1) / gridDim.x;
+    const size_t lo = min((size_t)blockIdx.x * per, n16) * 16;
+    const size_t hi = min(min((size_t)(blockIdx.x + 1) * per, n16) * 16, bytes);
+    if (threadIdx.x == 0) s_fail = 0;
+
+    // 1. copy-in of this block's share into this rank's scratch
+    if (hi > lo) block_copy<T>(a.my_scratch + lo, a.src + lo, hi - lo);
+    __syncthreads();
+
+    // 2. arrive at every peer, 3. wait for every peer
+    const int t = threadIdx.x;
+    if (t < a.P && t != a.rank)
+        st_release_sys(a.peer_flags[t] + a.rank * kMaxBlocks + blockIdx.x, a.epoch);
+    if (t < a.P && t != a.rank) {
+        uint32_t seen = 0;
+        unsigned long long deadline = globaltimer() + a.timeout_ns;
+        if (!wait_flag(a.my_flags + t * kMaxBlocks + blockIdx.x, a.epoch, deadline, &seen)) {
+            report(a.status, a.rank, t, blockIdx.x, a.epoch, seen);
+            s_fail = 1;
+        }
+    }
+    __syncthreads();
+    if (s_fail) return;
+
+    // 4. reduce the share from all P scratch copies in rank order
+    const size_t vlo = lo / 16, vhi = hi / 16;
+    const bool dst_vec = ((uintptr_t)a.dst & 15) == 0;
+    for (size_t i = vlo + threadIdx.x; i < vhi; i += blockDim.x) {
+        uint4 v[kMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+            if (q < a.P) v[q] = ld_v4(a.scratch[q] + i * 16);
+        uint4 acc = v[0];
+#pragma unroll
+        for (int q = 1; q < kMaxRanks; ++q)
+            if (q < a.P) acc = vop<OP, T>(acc, v[q]);
+        if (dst_vec) {
+            st_v4(a.dst + i * 16, acc);
+        } else {
+            const T *pa = reinterpret_cast<const T *>(&acc);
+#pragma unroll
+            for (int k = 0; k < (int)(16 / sizeof(T)); ++k)
+                reinterpret_cast<T *>(a.dst + i * 16)[k] = pa[k];
+        }
+    }
+    // ragged end (last block only)
+    for (size_t e = vhi * 16 / sizeof(T) + threadIdx.x; e < hi / sizeof(T); e += blockDim.x) {
+        T acc = reinterpret_cast<const T *>(a.scratch[0])[e];
+        for (int q = 1; q < a.P; ++q) acc = apply<OP, T>(acc, reinterpret_cast<const T *>(a.scratch[q])[e]);
+        reinterpret_cast<T *>(a.dst)[e] = acc;
+    }
+}
+
+// ---------------------------------------------------------------- two-shot
+template <int OP, typename T>
+__device__ __forceinline__ void scalar_elem(const TwoShotArgs &a, size_t e) {
+    T acc = reinterpret_cast<const T *>(a.src[0])[e];
+    for (int q = 1; q < a.P; ++q) acc = apply<OP, T>(acc, reinterpret_cast<const T *>(a.src[q])[e]);
+    for (int q = 0; q < a.P; ++q) reinterpret_cast<T *>(a.dst[q])[e] = acc;
+}
+
+template <int OP, typename T>
+__global__ void __launch_bounds__(512) twoshot_kernel(TwoShotArgs a) {
+    constexpr int V = 16 / sizeof(T);
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (a.vector_ok) {
+        const size_t lo = a.nvec * a.rank / a.P, hi = a.nvec * (a.rank + 1) / a.P;
+        const size_t base = a.head * sizeof(T);
+        for (size_t i = lo + tid; i < hi; i += stride) {
+            const size_t off = base + i * 16;
+            uint4 v[kMaxRanks];
+#pragma unroll
+            for (int q = 0; q < kMaxRanks; ++q)
+                if (q < a.P) v[q] = ld_v4(a.src[q] + off);
+            uint4 acc = v[0];
+#pragma unroll
+            for (int q = 1; q < kMaxRanks; ++q)
+                if (q < a.P) acc = vop<OP, T>(acc, v[q]);
+#pragma unroll
+            for (int q = 0; q < kMaxRanks; ++q)
+                if (q < a.P) st_v4(a.dst[q] + off, acc);
+        }
+        if (a.rank == 0) {
+            const size_t tail0 = a.head + a.nvec * V;
+            for (size_t e = tid; e < a.head; e += stride) scalar_elem<OP, T>(a, e);
+            for (size_t e = tail0 + tid; e < a.count; e += stride) scalar_elem<OP, T>(a, e);
+        }
+    } else {
+        const size_t lo = a.count * a.rank / a.P, hi = a.count * (a.rank + 1) / a.P;
+        for (size_t e = lo + tid; e < hi; e += stride) scalar_elem<OP, T>(a, e);
+    }
+    __threadfence_system();
+}
+
+// ---------------------------------------------------------------- NVLS
+// multimem forms accepted by ptxas for sm_100a (probed): add on u32, u64
+// (also serves s32/s64: wrapping addition has the same bits), f32 (also as
+// .v4) and f64; min/max on u32, s32, u64, s64.  No PROD, no 8/16-bit
+// integers, no floating-point min/max: those pairs stay on the P2P kernels.
+template <int OP, int EC> struct Mm { static constexpr bool ok = false; static constexpr int bytes = 16; };
+
+#define CAIL_MM_SCALAR(OPC, ECC, PTX, CT, CONS)                                                 \
+    template <> struct Mm<OPC, ECC> {                                                           \
+        static constexpr bool ok = true;                                                        \
+        static constexpr int bytes = sizeof(CT);                                                \
+        static __device__ __forceinline__ void run(char *mc) {                                  \
+            CT v;                                                                               \
+            asm volatile("multimem.ld_reduce.relaxed.sys.global." PTX " %0, [%1];"             \
+                         : "=" CONS(v) : "l"(mc) : "memory");                                   \
+            asm volatile("multimem.st.relaxed.sys.global." PTX_ST_##ECC " [%0], %1;"           \
+                         ::"l"(mc), CONS(v) : "memory");                                        \
+        }                                                                                       \
+    };
+#define PTX_ST_CAIL_EC_U32 "u32"
+#define PTX_ST_CAIL_EC_I32 "b32"
+#define PTX_ST_CAIL_EC_U64 "u64"
+#define PTX_ST_CAIL_EC_I64 "b64"
+#define PTX_ST_CAIL_EC_F64 "f64"
+
+CAIL_MM_SCALAR(CAIL_SUM, CAIL_EC_U32, "add.u32", unsigned, "r")
+CAIL_MM_SCALAR(CAIL_SUM, CAIL_EC_U64, "add.u64", unsigned long long, "l")
+CAIL_MM_SCALAR(CAIL_SUM, CAIL_EC_F64, "add.f64", double, "d")
+CAIL_MM_SCALAR(CAIL_MAX, CAIL_EC_U32, "max.u32", unsigned, "r")
+CAIL_MM_SCALAR(CAIL_MAX, CAIL_EC_I32, "max.s32", unsigned, "r")
+CAIL_MM_SCALAR(CAIL_MAX, CAIL_EC_U64, "max.u64", unsigned long long, "l")
+CAIL_MM_SCALAR(CAIL_MAX, CAIL_EC_I64, "max.s64", unsigned long long, "l")
+CAIL_MM_SCALAR(CAIL_MIN, CAIL_EC_U32, "min.u32", unsigned, "r")
+CAIL_MM_SCALAR(CAIL_MIN, CAIL_EC_I32, "min.s32", unsigned, "r")
+CAIL_MM_SCALAR(CAIL_MIN, CAIL_EC_U64, "min.u64", unsigned long long, "l")
+CAIL_MM_SCALAR(CAIL_MIN, CAIL_EC_I64, "min.s64", unsigned long long, "l")
+
+template <> struct Mm<CAIL_SUM, CAIL_EC_F32> {
+    static constexpr bool ok = true;
+    static constexpr int bytes = 16;
+    static __device__ __forceinline__ void run(char *mc) {
+        float a, b, c, d;
+        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
+                     : "=f"(a), "=f"(b), "=f"(c), "=f"(d) : "l"(mc) : "memory");
+        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};"
+                     ::"l"(mc), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+    }
+};
+
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+// Cross-rank + grid-wide barrier: one multimem.red per CTA, then wait for the
+// local counter.  Called by thread 0 only.
+__device__ __forceinline__ bool nvls_barrier(const NvlsArgs &a, uint32_t target, int which) {
+    asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.mc_counter), "r"(1u)
+                 : "memory");
+    uint32_t seen = 0;
+    unsigned long long deadline = globaltimer() + a.timeout_ns;
+    if (!wait_flag(a.uc_counter, target, deadline, &seen)) {
+        report(a.status, a.rank, -1 - which, blockIdx.x, target, seen);
+        return false;
+    }
+    return true;
+}
+
+template <typename T>
+__device__ __forceinline__ void grid_copy(char *dst, const char *src, size_t n) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if ((((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
+        const size_t nv = n / 16;
+        for (size_t i = tid; i < nv; i += stride)
+            st_v4(dst + i * 16, *reinterpret_cast<const uint4 *>(src + i * 16));
+        for (size_t e = nv * 16 / sizeof(T) + tid; e < n / sizeof(T); e += stride)
+            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+    } else {
+        for (size_t e = tid; e < n / sizeof(T); e += stride)
+            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+    }
+}
+
+template <int OP, int EC>
+__global__ void __launch_bounds__(512) nvls_kernel(NvlsArgs a) {
+    using T = typename EcType<EC>::T;
+    using M = Mm<OP, EC>;
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
+    const size_t bytes = a.count * sizeof(T);
+
+    grid_copy<T>(a.uc, a.src, bytes);  // copy-in
+    fence_proxy_alias();
+    __syncthreads();
+    if (threadIdx.x == 0 && !nvls_barrier(a, a.target_a, 0)) s_fail = 1;
+    __syncthreads();
+    if (s_fail) return;
+    fence_proxy_alias();
+
+    // this rank's slice of multimem units (the last unit may run past
+    // `count` into the staging padding; only `bytes` are copied out)
+    const size_t units = (bytes + M::bytes - 1) / M::bytes;
+    const size_t lo = units * a.rank / a.P, hi = units * (a.rank + 1) / a.P;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t u = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; u < hi; u += stride)
+        M::run(a.mc + u * M::bytes);
+    fence_proxy_alias();
+    __syncthreads();
+    if (threadIdx.x == 0 && !nvls_barrier(a, a.target_b, 1)) s_fail = 1;
+    __syncthreads();
+    if (s_fail) return;
+    fence_proxy_alias();
+
+    grid_copy<T>(a.dst, a.uc, bytes);  // copy-out
+}
+
+// ---------------------------------------------------------------- local reduce
+template <int OP, typename T>
+__global__ void __launch_bounds__(256) reduce_local_kernel(const T *__restrict__ in,
+                                                           T *__restrict__ io, size_t n,
+                                                           size_t head, size_t nvec, int vec) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (!vec) {
+        for (size_t e = tid; e < n; e += stride) io[e] = apply<OP, T>(io[e], in[e]);
+        return;
+    }
+    constexpr int V = 16 / sizeof(T);
+    const uint4 *vin = reinterpret_cast<const uint4 *>(in + head);
+    uint4 *vio = reinterpret_cast<uint4 *>(io + head);
+    for (size_t i = tid; i < nvec; i += stride) vio[i] = vop<OP, T>(vio[i], __ldg(vin + i));
+    for (size_t e = tid; e < head; e += stride) io[e] = apply<OP, T>(io[e], in[e]);
+    for (size_t e = head + nvec * V + tid; e < n; e += stride) io[e] = apply<OP, T>(io[e], in[e]);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- launchers
+// Functors for dispatch_op_class: one instantiation per (op, storage class).
+namespace {
+
+struct LaunchOneShot {
+    const OneShotArgs &a;
+    int b, t;
+    cudaStream_t s;
+    template <int OP, int EC> void operator()() {
+        oneshot_kernel<OP, typename EcType<EC>::T><<<b, t, 0, s>>>(a);
+    }
+};
+
+struct LaunchTwoShot {
+    const TwoShotArgs &a;
+    int b, t;
+    cudaStream_t s;
+    template <int OP, int EC> void operator()() {
+        twoshot_kernel<OP, typename EcType<EC>::T><<<b, t, 0, s>>>(a);
+    }
+};
+
+struct QueryNvls {
+    int ok = 0;
+    template <int OP, int EC> void operator()() { ok = Mm<OP, EC>::ok ? 1 : 0; }
+};
+
+struct LaunchNvls {
+    const NvlsArgs &a;
+    int b, t;
+    cudaStream_t s;
+    bool ok = false;
+    template <int OP, int EC> void operator()() {
+        if constexpr (Mm<OP, EC>::ok) {
+            nvls_kernel<OP, EC><<<b, t, 0, s>>>(a);
+            ok = true;
+        }
+    }
+};
+
+struct LaunchReduceLocal {
+    const void *in;
+    void *io;
+    size_t n;
+    int sms;
+    cudaStream_t s;
+    template <int OP, int EC> void operator()() {
+        using T = typename EcType<EC>::T;
+        constexpr int V = 16 / sizeof(T);
+        uintptr_t ai = (uintptr_t)in, ao = (uintptr_t)io;
+        int vec = (ai & 15) == (ao & 15);
+        size_t head = vec ? ((16 - (ao & 15)) & 15) / sizeof(T) : 0;
+        if (head > n) head = n;
+        size_t nvec = vec ? (n - head) / V : 0;
+        size_t work = vec ? nvec + 1 : n;
+        int threads = 256;
+        size_t want = (work + threads - 1) / threads;
+        int blocks = (int)(want < (size_t)sms * 8 ? want : (size_t)sms * 8);
+        if (blocks < 1) blocks = 1;
+        reduce_local_kernel<OP, T><<<blocks, threads, 0, s>>>((const T *)in, (T *)io, n, head, nvec,
+                                                             vec);
+    }
+};
+
+}  // namespace
+
+cudaError_t launch_oneshot(int op, int ec, const OneShotArgs &a, int blocks, int threads,
+                           cudaStream_t s) {
+    LaunchOneShot l{a, blocks, threads, s};
+    if (!dispatch_op_class(op, ec, l)) return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_twoshot(int op, int ec, const TwoShotArgs &a, int blocks, int threads,
+                           cudaStream_t s) {
+    LaunchTwoShot l{a, blocks, threads, s};
+    if (!dispatch_op_class(op, ec, l)) return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+int nvls_supported(int op, int ec) {
+    QueryNvls q;
+    if (!dispatch_op_class(op, ec, q)) return 0;
+    return q.ok;
+}
+
+cudaError_t launch_nvls(int op, int ec, const NvlsArgs &a, int blocks, int threads, cudaStream_t s) {
+    LaunchNvls l{a, blocks, threads, s};
+    if (!dispatch_op_class(op, ec, l) || !l.ok) return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_reduce_local(int op, int ec, const void *in, void *io, size_t n, int sm_count,
+                                cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    LaunchReduceLocal l{in, io, n, sm_count > 0 ? sm_count : 148, s};
+    if (!dispatch_op_class(op, ec, l)) return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+}  // namespace cail

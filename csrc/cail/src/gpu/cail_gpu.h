@@ -1,0 +1,42 @@
+// cail_gpu.h — backend seam between the algorithms and the memory they run on.
+//
+// The same nine entry points as the reference's backend interface
+// (src/gpu/cail_gpu.h:19-47 there), implemented by
+//   gpu/cuda/  CUDA runtime + sm_100a kernels (default build)
+//   gpu/host/  host memory and a templated host reduction (CAIL_HOST_PATH)
+// A ROCm backend would plug in here; none is built for B200.
+#pragma once
+
+#include <stddef.h>
+
+#include "../core/cail_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+int cail_gpu_is_device_pointer(const void *ptr);
+
+/* inout[i] = op(inout[i], in[i]) for i in [0, count) */
+int cail_gpu_reduce_local(const void *in, void *inout, size_t count, cail_datatype_t dtype,
+                          cail_op_t op);
+
+int cail_gpu_malloc(void **ptr, size_t size);
+int cail_gpu_free(void *ptr);
+
+/* Copy between device buffers or device<->host; returns after completion. */
+int cail_gpu_memcpy(void *dst, const void *src, size_t size);
+
+int cail_gpu_synchronize(void);
+
+/* Read fence after a network receive into device memory: a 1-byte
+ * device->host read of the last byte drains earlier posted writes (NIC RDMA,
+ * GDRCopy stores).  No-op when CAIL_FLUSH_RECV=0 or in the host build. */
+int cail_gpu_flush_recv_buf(const void *recv_buf, size_t recv_bytes);
+
+int cail_gpu_init(void);
+void cail_gpu_finalize(void);
+
+#ifdef __cplusplus
+}
+#endif

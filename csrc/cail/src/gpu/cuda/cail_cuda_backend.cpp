@@ -1,0 +1,129 @@
+// cail_cuda_backend.cpp — CUDA implementation of the backend seam.
+//
+// Covers what the reference splits over src/gpu/cuda/cail_cuda_mem.c and the
+// host half of src/gpu/cuda/cail_cuda_reduce.cu there: pointer
+// classification (device and managed memory count as device), allocation,
+// copies, the receive read-fence, and the local reduction used by the
+// point-to-point algorithms (kernel in dev/cail_dev_kernels.cu).  Work runs
+// on one non-blocking stream per device; every entry point returns after
+// its work completed, because MPI_Allreduce is blocking.
+#include <cuda_runtime.h>
+
+#include "../../core/cail_internal.h"
+#include "../../dev/cail_dev_kernels.cuh"
+#include "../cail_gpu.h"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+cudaStream_t g_stream[kMaxDevices] = {};
+int g_sms[kMaxDevices] = {};
+char *g_flush_byte = nullptr;
+int g_cuda = -1;  // -1 unknown, 0 absent, 1 present
+
+bool cuda_present() {
+    if (g_cuda < 0) {
+        int n = 0;
+        g_cuda = (cudaGetDeviceCount(&n) == cudaSuccess && n > 0) ? 1 : 0;
+        if (!g_cuda) cudaGetLastError();
+    }
+    return g_cuda == 1;
+}
+
+int current_device() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return d < 0 || d >= kMaxDevices ? 0 : d;
+}
+
+cudaStream_t stream() {
+    int d = current_device();
+    if (!g_stream[d]) {
+        cudaStreamCreateWithFlags(&g_stream[d], cudaStreamNonBlocking);
+        cudaDeviceGetAttribute(&g_sms[d], cudaDevAttrMultiProcessorCount, d);
+    }
+    return g_stream[d];
+}
+
+int sync_or_warn(const char *what) {
+    cudaError_t e = cudaStreamSynchronize(stream());
+    if (e != cudaSuccess) {
+        CAIL_WARN("%s: %s", what, cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cail_gpu_is_device_pointer(const void *ptr) {
+    if (!ptr || ptr == MPI_IN_PLACE || !cuda_present()) return 0;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) return 0;
+    // run the call on the buffer's device
+    if (a.device >= 0 && a.device != current_device()) cudaSetDevice(a.device);
+    return 1;
+}
+
+int cail_gpu_reduce_local(const void *in, void *inout, size_t count, cail_datatype_t dtype,
+                          cail_op_t op) {
+    if (op < 0 || op >= CAIL_NUM_OPS || dtype < 0 || dtype >= CAIL_NUM_DTYPES) {
+        CAIL_WARN("gpu_reduce_local: dtype=%d op=%d out of range", (int)dtype, (int)op);
+        return -1;
+    }
+    cudaStream_t s = stream();
+    cudaError_t e = cail::launch_reduce_local((int)op, (int)cail_elem_class(dtype), in, inout, count,
+                                              g_sms[current_device()], s);
+    if (e != cudaSuccess) {
+        CAIL_WARN("gpu_reduce_local: launch failed (%s) for dtype=%s op=%s count=%zu",
+                  cudaGetErrorString(e), cail_dtype_name(dtype), cail_op_name(op), count);
+        return -1;
+    }
+    return sync_or_warn("gpu_reduce_local: cudaStreamSynchronize failed");
+}
+
+int cail_gpu_malloc(void **ptr, size_t size) { return cudaMalloc(ptr, size) == cudaSuccess ? 0 : -1; }
+
+int cail_gpu_free(void *ptr) { return cudaFree(ptr) == cudaSuccess ? 0 : -1; }
+
+int cail_gpu_memcpy(void *dst, const void *src, size_t size) {
+    if (size == 0) return 0;
+    if (cudaMemcpyAsync(dst, src, size, cudaMemcpyDefault, stream()) != cudaSuccess) return -1;
+    return sync_or_warn("gpu_memcpy");
+}
+
+int cail_gpu_synchronize(void) { return sync_or_warn("gpu_synchronize"); }
+
+int cail_gpu_flush_recv_buf(const void *recv_buf, size_t recv_bytes) {
+    if (!cail_global_state.flush_recv || !g_flush_byte || !recv_buf || recv_bytes == 0) return 0;
+    cudaMemcpyAsync(g_flush_byte, (const char *)recv_buf + recv_bytes - 1, 1, cudaMemcpyDeviceToHost,
+                    stream());
+    cudaStreamSynchronize(stream());
+    return 0;
+}
+
+int cail_gpu_init(void) {
+    if (!cuda_present()) return 0;  // host-only buffers: every call passes through
+    if (!g_flush_byte && cudaHostAlloc((void **)&g_flush_byte, 1, cudaHostAllocDefault) != cudaSuccess) {
+        g_flush_byte = nullptr;
+        cudaGetLastError();
+    }
+    return 0;
+}
+
+void cail_gpu_finalize(void) {
+    if (g_flush_byte) cudaFreeHost(g_flush_byte);
+    g_flush_byte = nullptr;
+    for (int d = 0; d < kMaxDevices; ++d) {
+        if (g_stream[d]) cudaStreamDestroy(g_stream[d]);
+        g_stream[d] = nullptr;
+    }
+}
+
+}  // extern "C"
