@@ -1,0 +1,285 @@
+#!/usr/bin/env python
+"""Allreduce benchmark: bus bandwidth and p50 latency of MPI_Allreduce.
+
+Headline (one JSON line on rank 0): MPI_FLOAT SUM of a 1 GiB buffer per
+rank, separate send/recv buffers, inputs normal(0,1) seeded per rank; K
+timed calls after W warm-up calls, bracketed by a barrier and
+torch.cuda.synchronize() on both sides, timed with CUDA events, max over
+ranks.  1 GiB inputs exceed the 126 MB L2, so no flush is needed.  The
+JSON also carries the size sweep 32 KiB .. 1 GiB (busbw and p50 latency per
+size, max over ranks) and an end-to-end number through the public API that
+includes the host->device copy of each step's input from pinned memory and
+the device->host copy of its result.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|nccl|pmpi]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU)
+
+--impl reference runs the unmodified reference library (baseline/_ref,
+built by baseline/build_reference.py) through its own public API,
+MPI_Allreduce, on the same MPI; --impl nccl runs torch.distributed NCCL
+all_reduce; --impl pmpi runs the MPI's own PMPI_Allreduce (no interposer).
+
+busbw = 2 (P-1)/P * bytes / t (nccl-tests convention).  With one GPU that
+factor is 0, so the N=1 value is algbw = bytes / t of the single-rank call
+(a device copy through cail's kernels).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import time
+
+METRIC = "allreduce busbw GB/s & p50 latency vs msg size at 2/4/8 B200 (max over ranks)"
+GIB = 1 << 30
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def busbw(nbytes: int, t_s: float, p: int) -> float:
+    alg = nbytes / t_s / 1e9
+    return alg * 2 * (p - 1) / p if p > 1 else alg
+
+
+def unavailable(reason: str) -> None:
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+    sys.exit(0)
+
+
+class Comm:
+    """Barrier / max-over-ranks for either MPI (ours, reference, pmpi) or NCCL."""
+
+    def __init__(self, impl: str, rank: int, size: int):
+        self.impl = impl
+        self.rank = rank
+        self.size = size
+
+    def barrier(self):
+        if self.impl == "nccl":
+            import torch.distributed as dist
+            dist.barrier()
+        else:
+            import cail_b200
+            cail_b200.barrier()
+
+    def max(self, v: float) -> float:
+        if self.impl == "nccl":
+            import torch
+            import torch.distributed as dist
+            t = torch.tensor([v], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        import cail_b200
+        return cail_b200.host_max(v)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "nccl", "pmpi"])
+    ap.add_argument("--bytes", type=int, default=GIB, help="headline message size per rank")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--sweep-min", type=int, default=32 << 10)
+    ap.add_argument("--sweep-max", type=int, default=GIB)
+    ap.add_argument("--sweep-iters", type=int, default=100)
+    ap.add_argument("--sweep-warmup", type=int, default=20)
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log(f"bench: WORLD_SIZE={world} but --gpus {args.gpus}; launch with torchrun --nproc-per-node {args.gpus}")
+        sys.exit(2)
+    if args.warmup < 3:
+        log("bench: at least 3 warm-up steps are required; using 3")
+        args.warmup = 3
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    import torch
+
+    if args.impl == "reference":
+        from cail_b200 import _lib
+        if not os.path.exists(os.path.join(_lib.REF_LIB_DIR, "libcail.so")):
+            unavailable("reference library not built: run python baseline/build_reference.py "
+                        "(the reference is a C/autotools library with no Python packaging)")
+    torch.cuda.set_device(local)
+    torch.cuda.init()
+    dev = torch.device("cuda", local)
+
+    if args.impl == "nccl":
+        import torch.distributed as dist
+        from datetime import timedelta
+        if world > 1:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        comm = Comm("nccl", rank, world)
+
+        def allreduce(src, dst):
+            if world > 1:
+                dist.all_reduce(dst)
+            else:
+                dst.copy_(src)
+    else:
+        import cail_b200
+        from cail_b200 import _lib
+        impl = {"ours": "ours", "reference": "reference", "pmpi": "none"}[args.impl]
+        cail_b200.init(impl)
+        comm = Comm(args.impl, cail_b200.rank(), cail_b200.world_size())
+        libs = _lib.loaded()
+        H = _lib.H
+        import ctypes
+
+        def allreduce(src, dst):
+            rc = libs.cail.MPI_Allreduce(ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(dst.data_ptr()),
+                                         src.numel(), H["MPI_FLOAT"], H["MPI_SUM"], H["MPI_COMM_WORLD"])
+            if rc != 0:
+                raise RuntimeError(f"MPI_Allreduce returned {rc}")
+
+    P = world
+    count = args.bytes // 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    send = torch.randn(count, device=dev, generator=gen)
+    recv = torch.empty_like(send)
+    torch.cuda.synchronize()
+
+    def stats_launches():
+        if args.impl != "ours":
+            return None
+        import cail_b200
+        return cail_b200.stats().launches
+
+    # ---------------- headline: K timed steps of the full message
+    for _ in range(args.warmup):
+        allreduce(send, recv)
+    from cail_b200.utils import ClockSampler
+    comm.barrier()
+    torch.cuda.synchronize()
+    l0 = stats_launches()
+    with ClockSampler(local) as clocks:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            allreduce(send, recv)
+        end.record()
+        torch.cuda.synchronize()
+    comm.barrier()
+    l1 = stats_launches()
+    t_step = comm.max(start.elapsed_time(end) / 1e3 / args.steps)
+    value = busbw(args.bytes, t_step, P)
+    clock_summary = clocks.summary()
+    algo = None
+    if args.impl == "ours":
+        import cail_b200
+        algo = cail_b200.last_algorithm()
+
+    # ---------------- end to end through the public API, host data
+    e2e = None
+    if not args.no_e2e:
+        h_in = torch.empty(count, dtype=torch.float32, pin_memory=True)
+        h_in.copy_(send.cpu())
+        h_out = torch.empty(count, dtype=torch.float32, pin_memory=True)
+        for _ in range(2):
+            send.copy_(h_in, non_blocking=True)
+            torch.cuda.synchronize()
+            allreduce(send, recv)
+            h_out.copy_(recv, non_blocking=True)
+            torch.cuda.synchronize()
+        comm.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            send.copy_(h_in, non_blocking=True)
+            torch.cuda.synchronize()
+            allreduce(send, recv)
+            h_out.copy_(recv, non_blocking=True)
+            torch.cuda.synchronize()
+        t_e2e = comm.max((time.perf_counter() - t0) / args.steps)
+        e2e = {"value": busbw(args.bytes, t_e2e, P), "unit": "GB/s", "ms_per_step": t_e2e * 1e3,
+               "h2d_bytes_per_step": count * 4, "d2h_bytes_per_step": count * 4}
+        del h_in, h_out
+
+    # ---------------- sweep
+    sweep = []
+    if not args.no_sweep:
+        nbytes = args.sweep_min
+        while nbytes <= min(args.sweep_max, args.bytes):
+            n = nbytes // 4
+            s, r = send[:n], recv[:n]
+            iters = args.sweep_iters if nbytes <= (128 << 20) else max(10, args.sweep_iters // 5)
+            for _ in range(args.sweep_warmup):
+                allreduce(s, r)
+            comm.barrier()
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+            for a, b in evs:
+                a.record()
+                allreduce(s, r)
+                b.record()
+            torch.cuda.synchronize()
+            ts = [a.elapsed_time(b) / 1e3 for a, b in evs]
+            p50 = comm.max(statistics.median(ts))
+            p99 = comm.max(sorted(ts)[min(len(ts) - 1, int(math.ceil(0.99 * len(ts))) - 1)])
+            mean = comm.max(sum(ts) / len(ts))
+            row = {"bytes": nbytes, "busbw": round(busbw(nbytes, mean, P), 2), "p50_us": round(p50 * 1e6, 2),
+                   "p99_us": round(p99 * 1e6, 2)}
+            if args.impl == "ours":
+                import cail_b200
+                row["algo"] = cail_b200.last_algorithm()
+            sweep.append(row)
+            nbytes *= 2
+
+    out = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": P,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_step * 1e3, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic: normal(0,1) per element, seeded per rank",
+        "impl": args.impl,
+        "config": {
+            "model": "MPI_Allreduce MPI_FLOAT MPI_SUM (collective library; no model)",
+            "global_batch": count,
+            "seq_len": None,
+            "parallelism": f"allreduce over {P} rank(s), one per GPU",
+            "msg_bytes": args.bytes,
+            "buffers": "separate send/recv",
+            "l2": "inputs (1 GiB) larger than the 126 MB L2; sweep sizes below 128 MB are L2-warm",
+            "value_definition": ("busbw = 2(P-1)/P*bytes/t" if P > 1 else "algbw = bytes/t (busbw factor is 0 at P=1)"),
+            "timing": "CUDA events around K calls, barrier+synchronize both sides, max over ranks",
+        },
+        "clocks": clock_summary,
+        "e2e": e2e,
+        "gpu_launches": (l1 - l0) if (l0 is not None and l1 is not None) else None,
+        "algorithm": algo,
+        "sweep": sweep,
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+    if args.impl == "nccl":
+        import torch.distributed as dist
+        if world > 1:
+            dist.destroy_process_group()
+    else:
+        import cail_b200
+        cail_b200.finalize()
+
+
+if __name__ == "__main__":
+    main()

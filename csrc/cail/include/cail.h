@@ -40,6 +40,7 @@ typedef struct cail_stats {
     unsigned long long reg_hits;       /* registration cache hits (peer buffers) */
     unsigned long long reg_misses;     /* registration cache misses (IPC opens) */
     unsigned long long device_errors;  /* device collectives that reported an error */
+    unsigned long long launches;       /* CUDA kernels launched by cail */
 } cail_stats_t;
 int cail_get_stats(cail_stats_t *out);
 

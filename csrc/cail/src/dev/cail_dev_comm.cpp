@@ -170,6 +170,23 @@ struct Import {
 };
 constexpr size_t kMaxImports = 1024;
 
+// A process counts as gone when it no longer exists or is a zombie (it
+// exited and its parent has not reaped it yet).
+bool process_gone(int pid) {
+    if (pid <= 0) return false;
+    if (kill(pid, 0) != 0) return errno == ESRCH;
+    char path[64], buf[256];
+    snprintf(path, sizeof(path), "/proc/%d/stat", pid);
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) return false;
+    ssize_t n = read(fd, buf, sizeof(buf) - 1);
+    close(fd);
+    if (n <= 0) return false;
+    buf[n] = 0;
+    const char *rp = strrchr(buf, ')');
+    return rp && rp[1] == ' ' && (rp[2] == 'Z' || rp[2] == 'X');
+}
+
 unsigned long long host_id() {
     char h[256] = {0};
     gethostname(h, sizeof(h) - 1);
@@ -210,6 +227,7 @@ struct cail_dev_comm {
     uint32_t nvls_expected = 0;
     int nvls_blocks = 0;
     int nvls_next_half = 0;
+    double last_live_check = 0.0;
 };
 
 namespace {
@@ -250,8 +268,8 @@ int host_wait(cail_dev_comm *dc, bool depart, uint64_t seq) {
     for (int q = 0; q < dc->P; ++q) {
         std::atomic<uint64_t> &a = depart ? dc->xs[q].depart : dc->xs[q].arrive;
         while (a.load(std::memory_order_acquire) < seq) {
-            if (++spins % 4096 == 0) {
-                if (dc->peer_pid[q] > 0 && kill(dc->peer_pid[q], 0) != 0 && errno == ESRCH) {
+            if (++spins % 65536 == 0) {
+                if (process_gone(dc->peer_pid[q])) {
                     CAIL_ERR("rank %d: peer rank %d (pid %d) is gone", dc->rank, q, dc->peer_pid[q]);
                     return MPI_ERR_OTHER;
                 }
@@ -674,6 +692,7 @@ int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
         if (b >= 1 && b <= kMaxBlocks) blocks = b;
     }
     cudaError_t e = cail::launch_oneshot(op, ec, a, blocks, threads, dc->stream);
+    cail_counters.launches++;
     if (e != cudaSuccess) {
         CAIL_ERR("one_shot launch failed: %s", cudaGetErrorString(e));
         return MPI_ERR_OTHER;
@@ -745,6 +764,7 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
         int maxb = dc->sms * 2;
         int blocks = (int)(want < 1 ? 1 : (want > (size_t)maxb ? maxb : want));
         cudaError_t e = cail::launch_twoshot(op, ec, a, blocks, threads, dc->stream);
+        cail_counters.launches++;
         if (e != cudaSuccess) {
             CAIL_ERR("two_shot launch failed: %s", cudaGetErrorString(e));
             rc = MPI_ERR_OTHER;
@@ -788,6 +808,7 @@ int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
         a.timeout_ns = timeout_ns();
         a.status = dc->status_d;
         cudaError_t e = cail::launch_nvls(op, ec, a, blocks, 512, dc->stream);
+        cail_counters.launches++;
         if (e != cudaSuccess) {
             CAIL_ERR("nvls launch failed: %s", cudaGetErrorString(e));
             dc->broken = true;
@@ -840,7 +861,7 @@ int cail_dev_pick_algo(cail_dev_comm *dc, size_t bytes, int count, cail_datatype
     size_t one_max = s.oneshot_max ? s.oneshot_max
                                    : (s.msg_small_threshold_set ? s.msg_small_threshold - 1
                                                                 : default_oneshot_max(dc->P));
-    if (dc->P == 1 || bytes <= one_max) return CAIL_ALGO_ONE_SHOT;
+    if (bytes <= one_max) return CAIL_ALGO_ONE_SHOT;
     if (cail_dev_nvls_ok(dc, dt, op) && bytes >= nvls_min_bytes()) return CAIL_ALGO_NVLS;
     return CAIL_ALGO_TWO_SHOT;
 }
@@ -851,6 +872,20 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
         CAIL_ERR("nvlink context of this communicator failed earlier; refusing further calls");
         return MPI_ERR_OTHER;
     }
+    // A rank that left the job is noticed on the host before the next launch
+    // (checked at most every 10 ms, so back-to-back calls pay nothing).
+    double now = cail_now_us();
+    if (now - dc->last_live_check > 10000.0) {
+        dc->last_live_check = now;
+        for (int q = 0; q < dc->P; ++q) {
+            if (q != dc->rank && process_gone(dc->peer_pid[q])) {
+                CAIL_ERR("rank %d: peer rank %d (pid %d) has exited; not launching", dc->rank, q,
+                         dc->peer_pid[q]);
+                dc->broken = true;
+                return MPI_ERR_OTHER;
+            }
+        }
+    }
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != dc->dev) cudaSetDevice(dc->dev);
@@ -859,11 +894,8 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
     char *dst = (char *)recvbuf;
     const int ec = (int)cail_elem_class(dt);
     int rc = MPI_SUCCESS;
-    if (dc->P == 1) {
-        if (src != dst && cudaMemcpyAsync(dst, src, (size_t)count * esz, cudaMemcpyDefault, dc->stream) != cudaSuccess)
-            rc = MPI_ERR_OTHER;
-        if (rc == MPI_SUCCESS) rc = check_status(dc, "copy");
-    } else if (algo == CAIL_ALGO_ONE_SHOT) {
+    // A single rank runs the same kernels (they degenerate to a copy).
+    if (algo == CAIL_ALGO_ONE_SHOT) {
         rc = run_oneshot_chunked(dc, src, dst, (size_t)count, esz, (int)op, ec);
     } else if (algo == CAIL_ALGO_NVLS && cail_dev_nvls_ok(dc, dt, op)) {
         rc = run_nvls(dc, src, dst, (size_t)count, esz, (int)op, ec);
@@ -883,6 +915,47 @@ void cail_dev_finalize_all(void) {
     }
     g_contexts.clear();
     if (g_keyval != MPI_KEYVAL_INVALID) PMPI_Comm_free_keyval(&g_keyval);
+}
+
+// Self-test of the bounded device wait, on one GPU: a one-shot kernel for
+// two ranks whose peer never arrives (its flag is never written).  The
+// kernel must give up after timeout_ms and report DevStatus code 1; the
+// context stays usable.  Returns the status code, or -1 on a CUDA error.
+int cail_test_device_timeout(int timeout_ms) {
+    char *ws = nullptr;
+    DevStatus *st_h = nullptr, *st_d = nullptr;
+    cudaStream_t s = nullptr;
+    int code = -1;
+    const size_t half = 64 << 10;
+    if (cudaMalloc(&ws, kFlagBytes + 2 * half) == cudaSuccess &&
+        cudaMemset(ws, 0, kFlagBytes + 2 * half) == cudaSuccess &&
+        cudaHostAlloc((void **)&st_h, sizeof(DevStatus), cudaHostAllocMapped) == cudaSuccess &&
+        cudaHostGetDevicePointer((void **)&st_d, st_h, 0) == cudaSuccess &&
+        cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess) {
+        memset(st_h, 0, sizeof(DevStatus));
+        cail::OneShotArgs a;
+        memset(&a, 0, sizeof(a));
+        a.count = 1024;
+        a.src = ws + kFlagBytes;
+        a.dst = ws + kFlagBytes + half;
+        a.scratch[0] = a.scratch[1] = ws + kFlagBytes;
+        a.my_scratch = ws + kFlagBytes;
+        a.peer_flags[0] = a.peer_flags[1] = (uint32_t *)ws;
+        a.my_flags = (uint32_t *)ws;
+        a.P = 2;
+        a.rank = 0;
+        a.epoch = 1;
+        a.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+        a.status = st_d;
+        if (cail::launch_oneshot(CAIL_SUM, CAIL_EC_F32, a, 1, 128, s) == cudaSuccess &&
+            cudaStreamSynchronize(s) == cudaSuccess)
+            code = st_h->code;
+    }
+    cudaGetLastError();
+    if (s) cudaStreamDestroy(s);
+    if (st_h) cudaFreeHost(st_h);
+    if (ws) cudaFree(ws);
+    return code;
 }
 
 int cail_comm_uses_nvlink(MPI_Comm comm) {

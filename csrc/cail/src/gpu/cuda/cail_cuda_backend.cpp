@@ -80,6 +80,7 @@ int cail_gpu_reduce_local(const void *in, void *inout, size_t count, cail_dataty
     cudaStream_t s = stream();
     cudaError_t e = cail::launch_reduce_local((int)op, (int)cail_elem_class(dtype), in, inout, count,
                                               g_sms[current_device()], s);
+    cail_counters.launches++;
     if (e != cudaSuccess) {
         CAIL_WARN("gpu_reduce_local: launch failed (%s) for dtype=%s op=%s count=%zu",
                   cudaGetErrorString(e), cail_dtype_name(dtype), cail_op_name(op), count);

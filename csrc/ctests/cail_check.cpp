@@ -24,6 +24,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 #include <random>
 #include <string>
@@ -202,6 +203,18 @@ void mode_matrix(int base, double tol) {
             }
 }
 
+// Dtype/op coverage at the two acceptance counts: 1,000,003 (not divisible
+// by the world size) and 4,194,304; all 20 datatypes x SUM/PROD/MAX/MIN.
+void mode_config3(double tol) {
+    uint64_t seed = 77;
+    for (size_t c : {(size_t)1000003, (size_t)4194304})
+        for (const TypeCase &t : kTypes)
+            for (const OpCase &o : kOps) {
+                bool ok = check_one(t, o, c, false, seed++, tol);
+                report(ok, std::string(t.name) + " x " + o.name + " count=" + std::to_string(c));
+            }
+}
+
 void mode_edge() {
     // count = 0
     {
@@ -364,11 +377,37 @@ void mode_stress(int count, int reps, int nbuf, double tol) {
     for (auto *b : bufs) delete b;
 }
 
+// Rank 1 leaves the job between two allreduce steps (no collective in
+// flight); rank 0 must get an error from its next MPI_Allreduce instead of
+// waiting for it.  Exit 0 on rank 0 means the departure was detected.
+void mode_leave(int count) {
+    MPI_Comm_set_errhandler(MPI_COMM_WORLD, MPI_ERRORS_RETURN);
+    Buf s((size_t)count * 4), r((size_t)count * 4);
+    std::vector<float> h(count, 1.f);
+    s.put(h.data());
+    for (int it = 0; it < 6; ++it) {
+        if (g_rank == 1 && it == 2) {
+            fflush(stdout);
+            _exit(0);
+        }
+        if (g_rank == 0) usleep(100000);
+        int rc = MPI_Allreduce(s.p, r.p, count, MPI_FLOAT, MPI_SUM, MPI_COMM_WORLD);
+        if (rc != MPI_SUCCESS) {
+            if (g_rank == 0) printf("LEAVE DETECTED at step %d (rc=%d)\n", it, rc);
+            fflush(stdout);
+            _exit(it == 2 ? 0 : 4);
+        }
+    }
+    if (g_rank == 0) printf("LEAVE NOT DETECTED\n");
+    fflush(stdout);
+    _exit(5);
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
     std::string mode = "matrix";
-    int count = 1000, reps = 200, nbuf = 8;
+    int count = 0, reps = 200, nbuf = 8;
     double tol = 1e-5;
     for (int i = 1; i < argc; ++i) {
         std::string a = argv[i];
@@ -398,11 +437,13 @@ int main(int argc, char **argv) {
         if (!lr) lr = getenv("LOCAL_RANK");
         cudaSetDevice((lr ? atoi(lr) : g_rank) % n);
     }
-    if (mode == "basic") mode_basic(count > 0 && count != 1000 ? count : 0);
-    else if (mode == "matrix") mode_matrix(count, tol);
+    if (mode == "basic") mode_basic(count);
+    else if (mode == "matrix") mode_matrix(count ? count : 1000, tol);
     else if (mode == "edge") mode_edge();
+    else if (mode == "config3") mode_config3(tol);
     else if (mode == "config1") mode_config1(tol);
-    else if (mode == "stress") mode_stress(count, reps, nbuf, tol);
+    else if (mode == "stress") mode_stress(count ? count : 4096, reps, nbuf, tol);
+    else if (mode == "leave") mode_leave(count ? count : 65536);
     else { fprintf(stderr, "unknown mode %s\n", mode.c_str()); MPI_Abort(MPI_COMM_WORLD, 2); }
     if (g_rank == 0) printf("=== Results: %d passed, %d failed ===\n", g_pass, g_fail);
     MPI_Finalize();

@@ -287,6 +287,21 @@ void request_abort(int code) {
 }
 
 // ------------------------------------------------------------------ health
+// Gone = no such process, or a zombie its parent has not reaped yet.
+static bool process_gone(int pid) {
+    if (kill(pid, 0) != 0) return errno == ESRCH;
+    char path[64], buf[256];
+    snprintf(path, sizeof(path), "/proc/%d/stat", pid);
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) return false;
+    ssize_t n = read(fd, buf, sizeof(buf) - 1);
+    close(fd);
+    if (n <= 0) return false;
+    buf[n] = 0;
+    const char *rp = strrchr(buf, ')');
+    return rp && rp[1] == ' ' && (rp[2] == 'Z' || rp[2] == 'X');
+}
+
 int check_health() {
     Engine &e = g_engine;
     if (!e.base) return MPI_SUCCESS;
@@ -302,7 +317,7 @@ int check_health() {
         if (r == e.rank) continue;
         int32_t pid = e.slots[r].pid.load(std::memory_order_relaxed);
         uint32_t st = e.slots[r].state.load(std::memory_order_acquire);
-        if (pid > 0 && st == 1 && kill(pid, 0) != 0 && errno == ESRCH) {
+        if (pid > 0 && st == 1 && process_gone(pid)) {
             CMPI_ERR("peer rank %d (pid %d) exited without MPI_Finalize", r, pid);
             return MPI_ERR_PROC_FAILED;
         }

@@ -1,0 +1,148 @@
+"""GPU tests (B200).  Single-GPU tests run everywhere a GPU exists; the
+NVLink-kernel tests need two or more GPUs and skip otherwise.
+
+Oracle: minimpi's PMPI_Allreduce, which folds in rank order exactly like
+the one-shot and two-shot kernels, so their float results must match it
+bit for bit (--bits); NVLS reduces inside the switch in an unspecified
+order and is checked with a reassociation tolerance.
+"""
+import ctypes
+import os
+import subprocess
+import sys
+
+import pytest
+
+from conftest import LIB, ROOT, gpu_count, mpirun
+
+pytestmark = pytest.mark.gpu
+
+
+def ok(r):
+    return r.returncode == 0 and ", 0 failed" in r.stdout
+
+
+def need_gpus(n):
+    if gpu_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+
+
+# ---------------------------------------------------------------- one GPU
+def test_smoke_entry():
+    need_gpus(1)
+    r = subprocess.run([sys.executable, "-c", "import __graft_entry__ as g; g.smoke()"], cwd=ROOT,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "smoke ok" in r.stdout
+
+
+def test_native_library_loaded_in_process():
+    need_gpus(1)
+    code = ("import cail_b200 as c, torch; c.init(); x=torch.ones(1<<20, device='cuda');"
+            "c.ops.allreduce_(x); print(open('/proc/self/maps').read()); c.finalize()")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    assert os.path.join(LIB, "libcail.so") in r.stdout
+
+
+@pytest.mark.parametrize("algo", ["one_shot", "two_shot"])
+def test_single_rank_kernels_all_types(algo):
+    need_gpus(1)
+    r = mpirun(1, ["cail_check", "-m", "matrix", "-c", "100003", "-d", "-p", "--bits"], preload="cuda",
+               env={"CAIL_ALGO": algo, "CAIL_MIN_MSG_SIZE": "0"})
+    assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.parametrize("algo", ["recursive_doubling", "ring", "rabenseifner", "auto"])
+@pytest.mark.parametrize("np", [2, 3])
+def test_p2p_algorithms_device_buffers_one_gpu(algo, np):
+    """Several ranks on one GPU: no NVLink path (shared GPU), so the
+    point-to-point algorithms run on device buffers over minimpi's CUDA-IPC
+    transport, folding with the sm_100a local reduction kernel."""
+    need_gpus(1)
+    r = mpirun(np, ["cail_check", "-m", "matrix", "-c", "4099", "-d", "-p"], preload="cuda",
+               env={"CAIL_ALGO": algo, "CAIL_MIN_MSG_SIZE": "0", "CUDA_VISIBLE_DEVICES": "0"}, timeout=900)
+    assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_device_wait_timeout_reports_status():
+    """A one-shot kernel whose peer never arrives gives up after the limit
+    and reports code 1; the context stays usable afterwards."""
+    need_gpus(1)
+    code = ("import ctypes, time, torch; torch.cuda.init(); "
+            f"lib=ctypes.CDLL('{os.path.join(LIB, 'libmpi.so')}', mode=ctypes.RTLD_GLOBAL); "
+            f"c=ctypes.CDLL('{os.path.join(LIB, 'libcail.so')}'); t=time.time(); "
+            "rc=c.cail_test_device_timeout(300); dt=time.time()-t; "
+            "x=torch.ones(4, device='cuda'); torch.cuda.synchronize(); print(rc, dt, float(x.sum()))")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    rc, dt, s = r.stdout.split()
+    assert int(rc) == 1 and 0.25 < float(dt) < 30 and float(s) == 4.0
+
+
+def test_reference_sm100a_build_runs_on_device_buffers():
+    need_gpus(1)
+    if not os.path.exists(os.path.join(ROOT, "baseline", "_ref", "lib", "libcail.so")):
+        pytest.skip("reference baseline not built")
+    r = mpirun(2, ["cail_check", "-m", "config1", "-d"], preload="ref-cuda",
+               env={"CUDA_VISIBLE_DEVICES": "0"}, timeout=600)
+    assert ok(r), r.stdout[-2000:] + r.stderr[-2000:]
+
+
+# ---------------------------------------------------------------- NVLink kernels
+def nranks():
+    return [n for n in (2, 4, 8) if n <= gpu_count()]
+
+
+@pytest.mark.multigpu
+@pytest.mark.parametrize("algo", ["one_shot", "two_shot"])
+def test_nvlink_p2p_matrix_bit_exact(algo):
+    # counts {1,2,3,4099,4100,4102}: heads, tails, fewer elements than ranks;
+    # separate and in place; floats bit-identical to the rank-order oracle
+    need_gpus(2)
+    for np in nranks():
+        r = mpirun(np, ["cail_check", "-m", "matrix", "-c", "4099", "-d", "-p", "--bits"], preload="cuda",
+                   env={"CAIL_ALGO": algo, "CAIL_MIN_MSG_SIZE": "0"}, timeout=1200)
+        assert ok(r), f"np={np}\n" + r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.multigpu
+@pytest.mark.parametrize("algo", ["auto", "nvls", "two_shot"])
+def test_nvlink_config3_coverage(algo):
+    """20 datatypes x SUM/PROD/MAX/MIN at counts 1,000,003 and 4,194,304 at
+    every available rank count; integers bit-exact, floats within
+    reassociation tolerance (NVLS) or bit-exact (two-shot)."""
+    need_gpus(2)
+    for np in nranks():
+        args = ["cail_check", "-m", "config3", "-d"] + (["--bits"] if algo == "two_shot" else ["--tol", "1e-4"])
+        r = mpirun(np, args, preload="cuda", env={"CAIL_ALGO": algo}, timeout=1200)
+        assert ok(r), f"np={np} algo={algo}\n" + r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.multigpu
+def test_nvlink_edge_and_config1():
+    need_gpus(2)
+    for np in nranks():
+        r = mpirun(np, ["cail_check", "-m", "edge", "-d"], preload="cuda", timeout=600)
+        assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+        r = mpirun(np, ["cail_check", "-m", "config1", "-d"], preload="cuda", timeout=600)
+        assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.multigpu
+def test_registration_cache_stress():
+    need_gpus(2)
+    np = nranks()[-1]
+    for count in (4096, 32768, 1 << 20):
+        r = mpirun(np, ["cail_check", "-m", "stress", "-c", str(count), "-r", "300", "-b", "64", "-d", "--bits"],
+                   preload="cuda", env={"CAIL_STATS": "1", "CAIL_NVLS": "0"}, timeout=900)
+        assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.multigpu
+def test_rank_leaving_between_steps_is_detected():
+    need_gpus(2)
+    r = mpirun(2, ["cail_check", "-m", "leave", "-d"], preload="cuda",
+               env={"CAIL_NVLS": "0", "NCCL_NVLS_ENABLE": "0", "CAIL_DEVICE_TIMEOUT_MS": "1000"}, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "LEAVE DETECTED at step 2" in r.stdout
