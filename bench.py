@@ -79,8 +79,81 @@ class Comm:
         return cail_b200.host_max(v)
 
 
+def run_ddp(args, rank: int, world: int, local: int, comm: "Comm") -> dict:
+    """Data-parallel GPT-2-medium step: fp32, micro-batch 8 x 1024 tokens per
+    GPU, gradients in 25 MB buckets all-reduced through the interposer while
+    backward runs.  Exposed communication = step time with communication
+    minus step time of the same loop with the allreduces switched off."""
+    import torch
+
+    from cail_b200.models import GPT2, GPT2Config
+    from cail_b200.parallel import BucketedAllreduce
+
+    cfg = GPT2Config.medium()
+    mb, seq = args.micro_batch, cfg.n_ctx
+    torch.manual_seed(0)
+    model = GPT2(cfg).cuda()
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    ddp = BucketedAllreduce(model, world, bucket_bytes=25 << 20)
+    g = torch.Generator().manual_seed(4242 + rank)
+    host_x = torch.randint(0, cfg.vocab, (mb, seq), generator=g).pin_memory()
+    host_y = torch.randint(0, cfg.vocab, (mb, seq), generator=g).pin_memory()
+    x = torch.empty_like(host_x, device="cuda")
+    y = torch.empty_like(host_y, device="cuda")
+    on = ddp.enabled
+
+    def step():
+        ddp.zero_grad()
+        x.copy_(host_x, non_blocking=True)
+        y.copy_(host_y, non_blocking=True)
+        loss = model(x, y)
+        loss.backward()
+        ddp.finish()
+        opt.step()
+        return loss.item()  # device->host read of the step's result
+
+    def timed(enabled: bool) -> float:
+        ddp.enabled = enabled and on
+        comm.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        return comm.max((time.perf_counter() - t0) / args.steps)
+
+    for _ in range(args.warmup):
+        step()
+    ddp.check_views(model)
+    t_compute = timed(False)
+    t_full = timed(True)
+    ddp.close()
+    tokens = world * mb * seq
+    return {
+        "metric": "DDP GPT-2-medium training throughput (tokens/s, fp32 grads, 25 MB buckets)",
+        "value": round(tokens / t_full, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_full * 1e3, 3),
+        "compute_only_ms_per_step": round(t_compute * 1e3, 3),
+        "exposed_comm_ms": round((t_full - t_compute) * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "dtype": "fp32",
+        "data": "synthetic token ids uniform over the vocabulary; random-init weights",
+        "config": {"model": "GPT-2 medium (24L, d1024, 16H, MLP 4096, vocab 50257)", "global_batch": world * mb,
+                   "seq_len": seq, "parallelism": f"dp{world}", "buckets": ddp.num_buckets,
+                   "params": model.num_params()},
+        "impl": args.impl,
+    }
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", default="allreduce", choices=["allreduce", "ddp"])
+    ap.add_argument("--micro-batch", type=int, default=8)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
@@ -145,6 +218,16 @@ def main() -> None:
                 raise RuntimeError(f"MPI_Allreduce returned {rc}")
 
     P = world
+    if args.workload == "ddp":
+        if args.impl == "nccl":
+            log("bench: the ddp workload runs through MPI_Allreduce (ours, reference or pmpi)")
+            sys.exit(2)
+        out = run_ddp(args, rank, world, local, comm)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        import cail_b200
+        cail_b200.finalize()
+        return
     count = args.bytes // 4
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)

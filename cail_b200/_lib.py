@@ -101,7 +101,6 @@ def load(impl: str = "ours", host: bool = False) -> Libs:
     mpi_path = lib_path("libmpi.so")
     if not os.path.exists(mpi_path):
         raise FileNotFoundError(f"{mpi_path} missing: run cail_b200.build.build_native() first")
-    mpi = ctypes.CDLL(mpi_path, mode=ctypes.RTLD_GLOBAL)
     name = "libcail_host.so" if host else "libcail.so"
     if impl == "ours":
         path = lib_path(name)
@@ -113,7 +112,12 @@ def load(impl: str = "ours", host: bool = False) -> Libs:
         raise ValueError(impl)
     if not os.path.exists(path):
         raise FileNotFoundError(f"{path} missing")
-    cail = mpi if impl == "none" else ctypes.CDLL(path, mode=ctypes.RTLD_GLOBAL)
+    # The interposer goes into the global scope before libmpi (its
+    # dependency), so later global lookups of MPI_Allreduce find it first.
+    cail = None if impl == "none" else ctypes.CDLL(path, mode=ctypes.RTLD_GLOBAL)
+    mpi = ctypes.CDLL(mpi_path, mode=ctypes.RTLD_GLOBAL)
+    if cail is None:
+        cail = mpi
     _setup(mpi)
     _setup(cail)
     if impl == "ours":

@@ -51,6 +51,14 @@ int cail_comm_uses_nvlink(MPI_Comm comm);
 /* 1 if NVLS (NVSwitch multicast) is active on `comm`, else 0. */
 int cail_comm_uses_nvls(MPI_Comm comm);
 
+/* Stream ordering of device calls.  1 (default, env CAIL_STREAM_SYNC): cail
+ * first waits for all work already queued on the legacy default stream,
+ * which covers a cudaMemcpy from pageable memory whose DMA may still be in
+ * flight when it returns.  0: the caller guarantees that the buffers are
+ * complete (e.g. it synchronised the producing stream), which lets cail's
+ * kernels overlap later work on other streams.  Returns the previous mode. */
+int cail_set_stream_sync(int mode);
+
 #ifdef __cplusplus
 }
 #endif

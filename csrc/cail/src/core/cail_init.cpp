@@ -28,10 +28,13 @@ cail_state_t cail_global_state = {
     /*min_msg_size*/ CAIL_DEFAULT_MIN_MSG_SIZE,
     /*force_algo*/ CAIL_ALGO_AUTO,
     /*device_timeout_ms*/ CAIL_DEFAULT_DEVICE_TIMEOUT_MS,
-    /*nvls*/ 1, /*oneshot_max*/ 0, /*flush_recv*/ 1, /*stats*/ 0, /*trace*/ nullptr};
+    /*nvls*/ 1, /*oneshot_max*/ 0, /*flush_recv*/ 1, /*stats*/ 0, /*trace*/ nullptr,
+    /*stream_sync*/ 1, /*profile*/ 0};
 
 cail_stats_t cail_counters;
 int cail_last_algo = -2;  // -2: none yet, -3: passthrough
+double cail_prof_us[CAIL_PH_N];
+unsigned long long cail_prof_calls = 0;
 
 }  // extern "C"
 
@@ -54,6 +57,8 @@ const char *env_nonempty(const char *name) {
     return (v && v[0] != '\0') ? v : nullptr;
 }
 
+bool g_stream_sync_set = false;  // cail_set_stream_sync() overrides the environment
+
 }  // namespace
 
 extern "C" {
@@ -62,6 +67,13 @@ double cail_now_us(void) {
     struct timespec ts;
     clock_gettime(CLOCK_MONOTONIC, &ts);
     return ts.tv_sec * 1e6 + ts.tv_nsec * 1e-3;
+}
+
+double cail_prof_mark(int ph, double t0) {
+    if (!cail_global_state.profile) return t0;
+    double t = cail_now_us();
+    cail_prof_us[ph] += t - t0;
+    return t;
 }
 
 int cail_init(MPI_Comm comm) {
@@ -117,6 +129,8 @@ int cail_init(MPI_Comm comm) {
         s.oneshot_max = parse_long(CAIL_ENV_ONESHOT_MAX, e, 0, LONG_MAX, &v) ? (size_t)v : 0;
     if ((e = env_nonempty(CAIL_ENV_FLUSH_RECV))) s.flush_recv = e[0] != '0';
     if ((e = env_nonempty(CAIL_ENV_STATS))) s.stats = e[0] != '0';
+    if ((e = env_nonempty("CAIL_PROFILE"))) s.profile = e[0] != '0';
+    if ((e = env_nonempty(CAIL_ENV_STREAM_SYNC)) && !g_stream_sync_set) s.stream_sync = e[0] != '0';
     if ((e = env_nonempty(CAIL_ENV_TRACE))) {
         s.trace = fopen(e, "a");
         if (!s.trace) CAIL_ERR("cannot open CAIL_TRACE file '%s'", e);
@@ -147,6 +161,15 @@ void cail_finalize(void) {
                 c.calls, c.passthrough, c.by_algo[1], c.by_algo[2], c.by_algo[3], c.by_algo[4],
                 c.by_algo[5], c.by_algo[6], c.bytes, c.reg_hits, c.reg_misses, c.device_errors);
     }
+    if (s.profile && cail_prof_calls) {
+        const double n = (double)cail_prof_calls;
+        fprintf(stderr,
+                "[cail] profile: %llu calls, mean us: filter=%.2f setup=%.2f launch=%.2f wait=%.2f "
+                "hostsync=%.2f total=%.2f\n",
+                cail_prof_calls, cail_prof_us[CAIL_PH_FILTER] / n, cail_prof_us[CAIL_PH_SETUP] / n,
+                cail_prof_us[CAIL_PH_LAUNCH] / n, cail_prof_us[CAIL_PH_WAIT] / n,
+                cail_prof_us[CAIL_PH_HOSTSYNC] / n, cail_prof_us[CAIL_PH_TOTAL] / n);
+    }
     cail_gpu_finalize();
     cail_buf_finalize();
     if (s.trace) { fclose(s.trace); s.trace = nullptr; }
@@ -175,6 +198,13 @@ const char *cail_last_algorithm(void) {
     if (cail_last_algo == -2) return "none";
     if (cail_last_algo == -3) return "pmpi";
     return cail_algo_name(cail_last_algo);
+}
+
+int cail_set_stream_sync(int mode) {
+    int prev = cail_global_state.stream_sync;
+    cail_global_state.stream_sync = mode ? 1 : 0;
+    g_stream_sync_set = true;
+    return prev;
 }
 
 int cail_get_stats(cail_stats_t *out) {

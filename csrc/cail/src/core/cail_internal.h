@@ -36,6 +36,7 @@
 #define CAIL_ENV_STATS "CAIL_STATS"
 #define CAIL_ENV_TRACE "CAIL_TRACE"
 #define CAIL_ENV_FLUSH_RECV "CAIL_FLUSH_RECV"
+#define CAIL_ENV_STREAM_SYNC "CAIL_STREAM_SYNC"
 
 #define CAIL_DEFAULT_MSG_SMALL_THRESHOLD 262144U /* 256 KiB */
 #define CAIL_DEFAULT_NPROCS_THRESHOLD 4U
@@ -65,7 +66,21 @@ typedef struct cail_state {
     int flush_recv;
     int stats;
     FILE *trace;
+    int stream_sync;             /* order device work after the legacy stream */
+    int profile;                 /* CAIL_PROFILE: host-side phase timers */
 } cail_state_t;
+
+/* Opt-in host-side phase timers (CAIL_PROFILE=1), averaged per call and
+ * printed at MPI_Finalize. */
+enum {
+    CAIL_PH_FILTER = 0,  /* shim: entry to dispatch (type/op/pointer checks) */
+    CAIL_PH_SETUP,       /* dispatch + context lookup + argument preparation */
+    CAIL_PH_LAUNCH,      /* kernel launch calls */
+    CAIL_PH_WAIT,        /* waiting for the kernels (stream synchronise) */
+    CAIL_PH_HOSTSYNC,    /* host barriers of the two-shot path */
+    CAIL_PH_TOTAL,       /* whole intercepted call */
+    CAIL_PH_N
+};
 
 #ifdef __cplusplus
 extern "C" {
@@ -74,6 +89,11 @@ extern "C" {
 extern cail_state_t cail_global_state;
 extern cail_stats_t cail_counters;
 extern int cail_last_algo;
+extern double cail_prof_us[CAIL_PH_N];
+extern unsigned long long cail_prof_calls;
+
+/* Adds now - t0 to phase ph when profiling; returns now (or t0 when off). */
+double cail_prof_mark(int ph, double t0);
 
 int cail_init(MPI_Comm comm);
 void cail_finalize(void);

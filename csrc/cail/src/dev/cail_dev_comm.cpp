@@ -228,6 +228,7 @@ struct cail_dev_comm {
     int nvls_blocks = 0;
     int nvls_next_half = 0;
     double last_live_check = 0.0;
+    cudaEvent_t legacy_ev = nullptr;  // marks the legacy stream's queue at call entry
 };
 
 namespace {
@@ -316,6 +317,21 @@ char *import_buf(cail_dev_comm *dc, int q, const BufDesc &d) {
     }
     void *base = nullptr;
     cudaError_t e = cudaIpcOpenMemHandle(&base, d.handle, cudaIpcMemLazyEnablePeerAccess);
+    if (e == cudaErrorAlreadyMapped) {
+        // The peer freed an allocation that is still mapped here and reused
+        // its memory: drop this peer's mappings and open again.
+        cudaGetLastError();
+        for (auto i = dc->imports.begin(); i != dc->imports.end();) {
+            if (i->first.peer == q) {
+                cudaIpcCloseMemHandle(i->second.base);
+                dc->lru.erase(i->second.lru);
+                i = dc->imports.erase(i);
+            } else {
+                ++i;
+            }
+        }
+        e = cudaIpcOpenMemHandle(&base, d.handle, cudaIpcMemLazyEnablePeerAccess);
+    }
     if (e != cudaSuccess) {
         CAIL_ERR("rank %d: cannot open rank %d's buffer: %s", dc->rank, q, cudaGetErrorString(e));
         cudaGetLastError();
@@ -526,6 +542,7 @@ void destroy_context(cail_dev_comm *dc) {
         if (dc->ws) cudaFree(dc->ws);
         if (dc->status_h) cudaFreeHost(dc->status_h);
         if (dc->stream) cudaStreamDestroy(dc->stream);
+        if (dc->legacy_ev) cudaEventDestroy(dc->legacy_ev);
         if (dc->xs) munmap(dc->xs, dc->xs_bytes);
         if (prev >= 0) cudaSetDevice(prev);
     }
@@ -581,6 +598,7 @@ cail_dev_comm *create_context(MPI_Comm comm) {
 
     // 2. workspace
     ok = cudaStreamCreateWithFlags(&dc->stream, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&dc->legacy_ev, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaMalloc(&dc->ws, kWorkspaceBytes) == cudaSuccess;
     ok = ok && cudaMemset(dc->ws, 0, kFlagBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
     ok = ok && cudaHostAlloc((void **)&dc->status_h, sizeof(DevStatus), cudaHostAllocMapped) == cudaSuccess;
@@ -640,7 +658,9 @@ cail_dev_comm *create_context(MPI_Comm comm) {
 }
 
 int check_status(cail_dev_comm *dc, const char *what) {
+    const double t0 = cail_global_state.profile ? cail_now_us() : 0.0;
     cudaError_t e = cudaStreamSynchronize(dc->stream);
+    cail_prof_mark(CAIL_PH_WAIT, t0);
     if (e != cudaSuccess) {
         CAIL_ERR("%s: CUDA error %s", what, cudaGetErrorString(e));
         dc->broken = true;
@@ -687,11 +707,15 @@ int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     int threads = 512;
     size_t want = (vec + 2 * threads - 1) / (2 * threads);
     int blocks = (int)(want < 1 ? 1 : (want > (size_t)kMaxBlocks ? kMaxBlocks : want));
-    if (const char *e = getenv("CAIL_ONESHOT_BLOCKS")) {
-        int b = atoi(e);
-        if (b >= 1 && b <= kMaxBlocks) blocks = b;
-    }
+    static const int forced_blocks = [] {
+        const char *e = getenv("CAIL_ONESHOT_BLOCKS");
+        int b = e ? atoi(e) : 0;
+        return (b >= 1 && b <= kMaxBlocks) ? b : 0;
+    }();
+    if (forced_blocks) blocks = forced_blocks;
+    double t = cail_global_state.profile ? cail_now_us() : 0.0;
     cudaError_t e = cail::launch_oneshot(op, ec, a, blocks, threads, dc->stream);
+    cail_prof_mark(CAIL_PH_LAUNCH, t);
     cail_counters.launches++;
     if (e != cudaSuccess) {
         CAIL_ERR("one_shot launch failed: %s", cudaGetErrorString(e));
@@ -714,11 +738,19 @@ int run_oneshot_chunked(cail_dev_comm *dc, const char *src, char *dst, size_t co
 // ---- two-shot over registered user buffers
 int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec) {
     XSlot &me = dc->xs[dc->rank];
+    // Peers read this rank's buffers as soon as it arrives, so its pending
+    // legacy-stream writes must have landed first.
+    if (cail_global_state.stream_sync && cudaEventSynchronize(dc->legacy_ev) != cudaSuccess) {
+        CAIL_ERR("two_shot: waiting for the legacy stream failed");
+        return MPI_ERR_OTHER;
+    }
     describe(dc, src, &me.send);
     describe(dc, dst, &me.recv);
     uint64_t seq = ++dc->xseq;
     me.arrive.store(seq, std::memory_order_release);
+    double th = cail_global_state.profile ? cail_now_us() : 0.0;
     int rc = host_wait(dc, false, seq);
+    th = cail_prof_mark(CAIL_PH_HOSTSYNC, th);
     if (rc != MPI_SUCCESS) return rc;
     bool all_ok = true;
     for (int q = 0; q < dc->P; ++q) all_ok = all_ok && dc->xs[q].send.ok && dc->xs[q].recv.ok;
@@ -763,7 +795,9 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
         size_t want = (work + threads - 1) / threads;
         int maxb = dc->sms * 2;
         int blocks = (int)(want < 1 ? 1 : (want > (size_t)maxb ? maxb : want));
+        double tl = cail_global_state.profile ? cail_now_us() : 0.0;
         cudaError_t e = cail::launch_twoshot(op, ec, a, blocks, threads, dc->stream);
+        cail_prof_mark(CAIL_PH_LAUNCH, tl);
         cail_counters.launches++;
         if (e != cudaSuccess) {
             CAIL_ERR("two_shot launch failed: %s", cudaGetErrorString(e));
@@ -775,7 +809,9 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     // depart: peers may only return (and reuse their buffers) once every
     // rank's kernel has finished reading and writing them
     me.depart.store(seq, std::memory_order_release);
+    th = cail_global_state.profile ? cail_now_us() : 0.0;
     int rc2 = host_wait(dc, true, seq);
+    cail_prof_mark(CAIL_PH_HOSTSYNC, th);
     return rc != MPI_SUCCESS ? rc : rc2;
 }
 
@@ -894,6 +930,10 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
     char *dst = (char *)recvbuf;
     const int ec = (int)cail_elem_class(dt);
     int rc = MPI_SUCCESS;
+    if (cail_global_state.stream_sync) {
+        cudaEventRecord(dc->legacy_ev, cudaStreamLegacy);
+        cudaStreamWaitEvent(dc->stream, dc->legacy_ev, 0);
+    }
     // A single rank runs the same kernels (they degenerate to a copy).
     if (algo == CAIL_ALGO_ONE_SHOT) {
         rc = run_oneshot_chunked(dc, src, dst, (size_t)count, esz, (int)op, ec);

@@ -36,8 +36,15 @@ int current_device() {
     return d < 0 || d >= kMaxDevices ? 0 : d;
 }
 
+// With stream ordering on (the default) the point-to-point path works on the
+// legacy stream, like the reference's blocking stream; these calls are
+// host-synchronous, so nothing is lost.
 cudaStream_t stream() {
     int d = current_device();
+    if (cail_global_state.stream_sync) {
+        if (!g_sms[d]) cudaDeviceGetAttribute(&g_sms[d], cudaDevAttrMultiProcessorCount, d);
+        return cudaStreamLegacy;
+    }
     if (!g_stream[d]) {
         cudaStreamCreateWithFlags(&g_stream[d], cudaStreamNonBlocking);
         cudaDeviceGetAttribute(&g_sms[d], cudaDevAttrMultiProcessorCount, d);

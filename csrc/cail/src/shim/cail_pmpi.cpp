@@ -39,6 +39,7 @@ int MPI_Allreduce(const void *sendbuf, void *recvbuf, int count, MPI_Datatype da
         }
     }
     cail_counters.calls++;
+    const double t_in = cail_global_state.profile ? cail_now_us() : 0.0;
     if (count == 0) return MPI_SUCCESS;
 
     if (!cail_type_supported(datatype)) {
@@ -75,8 +76,13 @@ int MPI_Allreduce(const void *sendbuf, void *recvbuf, int count, MPI_Datatype da
     }
 
     double t0 = cail_global_state.trace ? cail_now_us() : 0.0;
+    cail_prof_mark(CAIL_PH_FILTER, t_in);
     int may_fallback = 1;
     rc = cail_allreduce_dispatch_ex(sendbuf, recvbuf, count, datatype, op, comm, &may_fallback);
+    if (cail_global_state.profile) {
+        cail_prof_mark(CAIL_PH_TOTAL, t_in);
+        cail_prof_calls++;
+    }
     if (rc != MPI_SUCCESS) {
         if (!may_fallback) {
             CAIL_ERR("device allreduce failed (rc=%d); not retrying through PMPI", rc);

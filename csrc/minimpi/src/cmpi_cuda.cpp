@@ -56,8 +56,6 @@ std::unordered_map<ImportKey, Import, ImportKeyHash> g_imports;
 std::list<ImportKey> g_lru;
 constexpr size_t kMaxImports = 512;
 
-cudaStream_t g_streams[64] = {};
-
 void load_driver_entry_points() {
     cudaDriverEntryPointQueryResult q;
     void *fn = nullptr;
@@ -70,10 +68,13 @@ void load_driver_entry_points() {
         p_range = (PFN_range)fn;
 }
 
+// Copies run on the legacy default stream: they are then ordered after all
+// earlier legacy-stream work of the process, including the DMA of a
+// cudaMemcpy from pageable memory, which may still be in flight when that
+// call returns.  A private non-blocking stream could read stale data.
 cudaStream_t stream_for(int dev) {
-    if (dev < 0 || dev >= 64) return 0;
-    if (!g_streams[dev]) cudaStreamCreateWithFlags(&g_streams[dev], cudaStreamNonBlocking);
-    return g_streams[dev];
+    (void)dev;
+    return cudaStreamLegacy;
 }
 
 // Runs f with device `dev` current and restores the caller's device.
@@ -174,6 +175,21 @@ int ipc_pull(int src, const RndvDesc &d, void *dst, bool dst_dev, int dst_ordina
             cudaIpcMemHandle_t h;
             memcpy(&h, d.handle, sizeof(h));
             cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+            if (e == cudaErrorAlreadyMapped) {
+                // The sender freed an allocation we still map and reused its
+                // memory; drop our mappings of that sender and retry.
+                cudaGetLastError();
+                for (auto it = g_imports.begin(); it != g_imports.end();) {
+                    if (it->first.src == src) {
+                        cudaIpcCloseMemHandle(it->second.base);
+                        g_lru.erase(it->second.lru);
+                        it = g_imports.erase(it);
+                    } else {
+                        ++it;
+                    }
+                }
+                e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+            }
             if (e != cudaSuccess) {
                 CMPI_ERR("cudaIpcOpenMemHandle from rank %d failed: %s", src, cudaGetErrorString(e));
                 return MPI_ERR_OTHER;
@@ -209,10 +225,6 @@ void cuda_finalize() {
     g_imports.clear();
     g_lru.clear();
     g_exports.clear();
-    for (auto &s : g_streams) {
-        if (s) cudaStreamDestroy(s);
-        s = 0;
-    }
 }
 
 }  // namespace cmpi
