@@ -81,6 +81,7 @@ extern "C" int cail_allreduce_dispatch_ex(const void *sendbuf, void *recvbuf, in
     *may_fallback = 1;
     cail_datatype_t dtype = cail_mpi_type_to_dtype(datatype);
     cail_op_t optype = cail_mpi_op_to_optype(op);
+    (void)optype;  // used by the NVLink path only
     size_t msg = (size_t)count * (size_t)cail_type_size(dtype);
     int nprocs;
     PMPI_Comm_size(comm, &nprocs);

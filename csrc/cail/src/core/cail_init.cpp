@@ -69,11 +69,30 @@ double cail_now_us(void) {
     return ts.tv_sec * 1e6 + ts.tv_nsec * 1e-3;
 }
 
+// Phase times of the call in progress; folded into cail_prof_us by
+// cail_prof_end_call() unless the call took longer than CAIL_PROFILE_MAX_US
+// (default 500), which keeps one-time costs such as lazy kernel loading out
+// of the small-message averages.
+static double g_call_us[CAIL_PH_N];
+
 double cail_prof_mark(int ph, double t0) {
     if (!cail_global_state.profile) return t0;
     double t = cail_now_us();
-    cail_prof_us[ph] += t - t0;
+    g_call_us[ph] += t - t0;
     return t;
+}
+
+void cail_prof_end_call(double total_us) {
+    static const double cutoff = [] {
+        const char *e = getenv("CAIL_PROFILE_MAX_US");
+        return e ? atof(e) : 500.0;
+    }();
+    if (total_us <= cutoff) {
+        for (int i = 0; i < CAIL_PH_N; ++i) cail_prof_us[i] += g_call_us[i];
+        cail_prof_us[CAIL_PH_TOTAL] += total_us;
+        cail_prof_calls++;
+    }
+    for (int i = 0; i < CAIL_PH_N; ++i) g_call_us[i] = 0.0;
 }
 
 int cail_init(MPI_Comm comm) {
@@ -164,7 +183,7 @@ void cail_finalize(void) {
     if (s.profile && cail_prof_calls) {
         const double n = (double)cail_prof_calls;
         fprintf(stderr,
-                "[cail] profile: %llu calls, mean us: filter=%.2f setup=%.2f launch=%.2f wait=%.2f "
+                "[cail] profile: %llu calls, mean us: filter=%.2f order=%.2f launch=%.2f wait=%.2f "
                 "hostsync=%.2f total=%.2f\n",
                 cail_prof_calls, cail_prof_us[CAIL_PH_FILTER] / n, cail_prof_us[CAIL_PH_SETUP] / n,
                 cail_prof_us[CAIL_PH_LAUNCH] / n, cail_prof_us[CAIL_PH_WAIT] / n,

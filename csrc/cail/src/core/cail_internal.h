@@ -92,8 +92,10 @@ extern int cail_last_algo;
 extern double cail_prof_us[CAIL_PH_N];
 extern unsigned long long cail_prof_calls;
 
-/* Adds now - t0 to phase ph when profiling; returns now (or t0 when off). */
+/* Adds now - t0 to phase ph of the current call when profiling; returns now
+ * (or t0 when off).  cail_prof_end_call() closes the call. */
 double cail_prof_mark(int ph, double t0);
+void cail_prof_end_call(double total_us);
 
 int cail_init(MPI_Comm comm);
 void cail_finalize(void);

@@ -118,8 +118,9 @@ void load_driver() {
 
 // ---------------------------------------------------------------- constants
 constexpr size_t kFlagBytes = 64 << 10;                 // arrival flags (16 KiB used)
-constexpr size_t kScratchHalf = 4 << 20;                // one-shot scratch per half
-constexpr size_t kWorkspaceBytes = kFlagBytes + 2 * kScratchHalf;
+constexpr size_t kSlotBytes = 1 << 20;                  // one-shot: bytes per source slot
+constexpr size_t kScratchParity = kMaxRanks * kSlotBytes;  // one slot per source rank
+constexpr size_t kWorkspaceBytes = kFlagBytes + 2 * kScratchParity;
 constexpr size_t kNvlsCounterBytes = 2 << 20;           // counter page(s) of the multicast region
 constexpr size_t kDefaultNvlsHalf = 128ull << 20;       // NVLS staging per half
 
@@ -456,17 +457,33 @@ void nvls_teardown(cail_dev_comm *dc) {
     dc->nvls = false;
 }
 
-// Collective NVLS setup.  Leaves dc->nvls false (on every rank) on failure.
+// Collective NVLS setup.  Leaves dc->nvls false (on every rank) on failure;
+// with CAIL_DEBUG the failing step and its CUresult are printed.
+bool nvls_step(cail_dev_comm *dc, bool ok, CUresult r, const char *what) {
+    if (ok && r != CUDA_SUCCESS) {
+        CAIL_DBG("nvls: rank %d: %s failed (CUresult %d)", dc->rank, what, (int)r);
+        return false;
+    }
+    return ok;
+}
+
 void nvls_setup(cail_dev_comm *dc, bool all_capable) {
-    if (!all_capable || !cail_global_state.nvls || dc->P < 2) return;
-    if (!g_drv.multicastCreate || !g_drv.multicastBindMem || !g_drv.memCreate) return;
+    if (!cail_global_state.nvls || dc->P < 2) return;
+    if (!all_capable) {
+        CAIL_DBG("nvls: not every GPU reports CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED");
+        return;
+    }
+    if (!g_drv.multicastCreate || !g_drv.multicastBindMem || !g_drv.memCreate) {
+        CAIL_DBG("nvls: driver entry points missing");
+        return;
+    }
     size_t half = kDefaultNvlsHalf;
     if (const char *e = getenv("CAIL_NVLS_CHUNK")) {
         long v = atol(e);
         if (v >= (1 << 20)) half = (size_t)v;
     }
-    CUdevice cd;
-    bool ok = g_drv.deviceGet(&cd, dc->dev) == CUDA_SUCCESS;
+    CUdevice cd = 0;
+    bool ok = nvls_step(dc, true, g_drv.deviceGet(&cd, dc->dev), "cuDeviceGet");
     CUmulticastObjectProp mp;
     memset(&mp, 0, sizeof(mp));
     mp.numDevices = (unsigned)dc->P;
@@ -478,8 +495,10 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     ap.location.id = cd;
     size_t g1 = 0, g2 = 0;
     mp.size = kNvlsCounterBytes + 2 * half;
-    ok = ok && g_drv.multicastGetGranularity(&g1, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED) == CUDA_SUCCESS;
-    ok = ok && g_drv.memGetAllocationGranularity(&g2, &ap, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED) == CUDA_SUCCESS;
+    ok = nvls_step(dc, ok, g_drv.multicastGetGranularity(&g1, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED),
+                   "cuMulticastGetGranularity");
+    ok = nvls_step(dc, ok, g_drv.memGetAllocationGranularity(&g2, &ap, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED),
+                   "cuMemGetAllocationGranularity");
     size_t gran = g1 > g2 ? g1 : g2;
     if (gran == 0) gran = 2 << 20;
     size_t size = (kNvlsCounterBytes + 2 * half + gran - 1) / gran * gran;
@@ -490,41 +509,51 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
 
     int fd = -1;
     if (dc->rank == 0) {
-        ok = g_drv.multicastCreate(&dc->mc_handle, &mp) == CUDA_SUCCESS &&
-             g_drv.memExportToShareableHandle(&fd, dc->mc_handle, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0) == CUDA_SUCCESS;
+        ok = nvls_step(dc, true, g_drv.multicastCreate(&dc->mc_handle, &mp), "cuMulticastCreate");
+        ok = nvls_step(dc, ok,
+                       g_drv.memExportToShareableHandle(&fd, dc->mc_handle,
+                                                        CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0),
+                       "cuMemExportToShareableHandle");
     }
     if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }
     int myfd = share_fd(dc, fd);
     ok = myfd >= 0;
+    if (!ok) CAIL_DBG("nvls: rank %d: file descriptor exchange failed", dc->rank);
     if (ok && dc->rank != 0)
-        ok = g_drv.memImportFromShareableHandle(&dc->mc_handle, (void *)(uintptr_t)myfd,
-                                                CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR) == CUDA_SUCCESS;
+        ok = nvls_step(dc, ok,
+                       g_drv.memImportFromShareableHandle(&dc->mc_handle, (void *)(uintptr_t)myfd,
+                                                          CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR),
+                       "cuMemImportFromShareableHandle");
     if (myfd >= 0) close(myfd);
     if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }
-    ok = g_drv.multicastAddDevice(dc->mc_handle, cd) == CUDA_SUCCESS;
+    ok = nvls_step(dc, ok, g_drv.multicastAddDevice(dc->mc_handle, cd), "cuMulticastAddDevice");
     if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }  // every device added before binding
-    ok = g_drv.memCreate(&dc->phys_handle, size, &ap, 0) == CUDA_SUCCESS;
-    ok = ok && g_drv.multicastBindMem(dc->mc_handle, 0, dc->phys_handle, 0, size, 0) == CUDA_SUCCESS;
+    ok = nvls_step(dc, ok, g_drv.memCreate(&dc->phys_handle, size, &ap, 0), "cuMemCreate");
+    ok = nvls_step(dc, ok, g_drv.multicastBindMem(dc->mc_handle, 0, dc->phys_handle, 0, size, 0),
+                   "cuMulticastBindMem");
     dc->mc_bound = ok;
     CUmemAccessDesc acc;
     memset(&acc, 0, sizeof(acc));
     acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
     acc.location.id = cd;
     acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
-    ok = ok && g_drv.memAddressReserve(&dc->uc_va, size, gran, 0, 0) == CUDA_SUCCESS;
-    ok = ok && g_drv.memMap(dc->uc_va, size, 0, dc->phys_handle, 0) == CUDA_SUCCESS;
-    ok = ok && g_drv.memSetAccess(dc->uc_va, size, &acc, 1) == CUDA_SUCCESS;
-    ok = ok && g_drv.memAddressReserve(&dc->mc_va, size, gran, 0, 0) == CUDA_SUCCESS;
-    ok = ok && g_drv.memMap(dc->mc_va, size, 0, dc->mc_handle, 0) == CUDA_SUCCESS;
-    ok = ok && g_drv.memSetAccess(dc->mc_va, size, &acc, 1) == CUDA_SUCCESS;
-    ok = ok && cudaMemset((void *)dc->uc_va, 0, kNvlsCounterBytes) == cudaSuccess &&
-         cudaDeviceSynchronize() == cudaSuccess;
+    ok = nvls_step(dc, ok, g_drv.memAddressReserve(&dc->uc_va, size, gran, 0, 0), "cuMemAddressReserve(uc)");
+    ok = nvls_step(dc, ok, g_drv.memMap(dc->uc_va, size, 0, dc->phys_handle, 0), "cuMemMap(uc)");
+    ok = nvls_step(dc, ok, g_drv.memSetAccess(dc->uc_va, size, &acc, 1), "cuMemSetAccess(uc)");
+    ok = nvls_step(dc, ok, g_drv.memAddressReserve(&dc->mc_va, size, gran, 0, 0), "cuMemAddressReserve(mc)");
+    ok = nvls_step(dc, ok, g_drv.memMap(dc->mc_va, size, 0, dc->mc_handle, 0), "cuMemMap(mc)");
+    ok = nvls_step(dc, ok, g_drv.memSetAccess(dc->mc_va, size, &acc, 1), "cuMemSetAccess(mc)");
+    if (ok && (cudaMemset((void *)dc->uc_va, 0, kNvlsCounterBytes) != cudaSuccess ||
+               cudaDeviceSynchronize() != cudaSuccess)) {
+        CAIL_DBG("nvls: rank %d: clearing the counters failed", dc->rank);
+        ok = false;
+    }
     if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }
     // two 512-thread CTAs per SM are always co-resident, which the
     // grid-wide counter barrier of the NVLS kernel requires
     dc->nvls_blocks = dc->sms * 2;
     dc->nvls = true;
-    CAIL_DBG("nvls: multicast region of %zu bytes, staging 2 x %zu", size, half);
+    CAIL_DBG("nvls: multicast region of %zu bytes (granularity %zu), staging 2 x %zu", size, gran, half);
 }
 
 void destroy_context(cail_dev_comm *dc) {
@@ -693,12 +722,13 @@ int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     a.P = dc->P;
     a.rank = dc->rank;
     a.epoch = ++dc->epoch;
-    const size_t half = (a.epoch & 1) ? kScratchHalf : 0;
+    const size_t parity = (a.epoch & 1) ? kScratchParity : 0;
     for (int q = 0; q < dc->P; ++q) {
-        a.scratch[q] = dc->peer_ws[q] + kFlagBytes + half;
+        a.slot_out[q] = dc->peer_ws[q] + kFlagBytes + parity + (size_t)dc->rank * kSlotBytes;
         a.peer_flags[q] = (uint32_t *)dc->peer_ws[q];
     }
-    a.my_scratch = dc->ws + kFlagBytes + half;
+    a.slot_in = dc->ws + kFlagBytes + parity;
+    a.slot_bytes = kSlotBytes;
     a.my_flags = (uint32_t *)dc->ws;
     a.timeout_ns = timeout_ns();
     a.status = dc->status_d;
@@ -726,7 +756,7 @@ int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
 
 int run_oneshot_chunked(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz,
                         int op, int ec) {
-    size_t per = kScratchHalf / esz;
+    size_t per = kSlotBytes / esz;
     for (size_t off = 0; off < count; off += per) {
         size_t n = count - off < per ? count - off : per;
         int rc = run_oneshot(dc, src + off * esz, dst + off * esz, n, esz, op, ec, false);
@@ -793,7 +823,17 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
         size_t work = vec_ok ? a.nvec / dc->P + 1 : count / dc->P + 1;
         int threads = 512;
         size_t want = (work + threads - 1) / threads;
-        int maxb = dc->sms * 2;
+        static const int per_sm = [] {
+            const char *e = getenv("CAIL_TWOSHOT_CTAS_PER_SM");
+            int v = e ? atoi(e) : 2;
+            return v >= 1 && v <= 4 ? v : 2;
+        }();
+        static const int unroll2 = [] {
+            const char *e = getenv("CAIL_TWOSHOT_UNROLL");
+            return e && atoi(e) >= 2 ? 1 : 0;
+        }();
+        a.unroll2 = unroll2;
+        int maxb = dc->sms * per_sm;
         int blocks = (int)(want < 1 ? 1 : (want > (size_t)maxb ? maxb : want));
         double tl = cail_global_state.profile ? cail_now_us() : 0.0;
         cudaError_t e = cail::launch_twoshot(op, ec, a, blocks, threads, dc->stream);
@@ -930,10 +970,12 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
     char *dst = (char *)recvbuf;
     const int ec = (int)cail_elem_class(dt);
     int rc = MPI_SUCCESS;
+    const double ts = cail_global_state.profile ? cail_now_us() : 0.0;
     if (cail_global_state.stream_sync) {
         cudaEventRecord(dc->legacy_ev, cudaStreamLegacy);
         cudaStreamWaitEvent(dc->stream, dc->legacy_ev, 0);
     }
+    cail_prof_mark(CAIL_PH_SETUP, ts);
     // A single rank runs the same kernels (they degenerate to a copy).
     if (algo == CAIL_ALGO_ONE_SHOT) {
         rc = run_oneshot_chunked(dc, src, dst, (size_t)count, esz, (int)op, ec);
@@ -966,9 +1008,11 @@ int cail_test_device_timeout(int timeout_ms) {
     DevStatus *st_h = nullptr, *st_d = nullptr;
     cudaStream_t s = nullptr;
     int code = -1;
-    const size_t half = 64 << 10;
-    if (cudaMalloc(&ws, kFlagBytes + 2 * half) == cudaSuccess &&
-        cudaMemset(ws, 0, kFlagBytes + 2 * half) == cudaSuccess &&
+    // layout: [flags][src 16 KiB][dst 16 KiB][two 16 KiB slots]; the second
+    // "peer" slot and the peer flag array are local memory
+    const size_t part = 16 << 10;
+    if (cudaMalloc(&ws, kFlagBytes + 4 * part) == cudaSuccess &&
+        cudaMemset(ws, 0, kFlagBytes + 4 * part) == cudaSuccess &&
         cudaHostAlloc((void **)&st_h, sizeof(DevStatus), cudaHostAllocMapped) == cudaSuccess &&
         cudaHostGetDevicePointer((void **)&st_d, st_h, 0) == cudaSuccess &&
         cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess) {
@@ -977,9 +1021,11 @@ int cail_test_device_timeout(int timeout_ms) {
         memset(&a, 0, sizeof(a));
         a.count = 1024;
         a.src = ws + kFlagBytes;
-        a.dst = ws + kFlagBytes + half;
-        a.scratch[0] = a.scratch[1] = ws + kFlagBytes;
-        a.my_scratch = ws + kFlagBytes;
+        a.dst = ws + kFlagBytes + part;
+        a.slot_out[0] = ws + kFlagBytes + 2 * part;
+        a.slot_out[1] = ws + kFlagBytes + 3 * part;
+        a.slot_in = ws + kFlagBytes + 2 * part;
+        a.slot_bytes = part;
         a.peer_flags[0] = a.peer_flags[1] = (uint32_t *)ws;
         a.my_flags = (uint32_t *)ws;
         a.P = 2;

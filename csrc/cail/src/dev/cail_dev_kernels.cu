@@ -88,23 +88,30 @@ __device__ void report(DevStatus *st, int rank, int peer, int block, uint32_t ep
     }
 }
 
-// Copies bytes [0, n) from src to dst (dst 16-byte aligned); src may be
-// unaligned, in which case the copy goes element by element.
+// ---------------------------------------------------------------- one-shot
+// Pushes bytes [lo, hi) of src (any alignment) into P destinations (16-byte
+// aligned slots), 16 bytes at a time where src allows it.
 template <typename T>
-__device__ __forceinline__ void block_copy(char *dst, const char *src, size_t n) {
+__device__ __forceinline__ void block_push(char *const *dst, int P, const char *src, size_t lo, size_t hi) {
     if (((uintptr_t)src & 15) == 0) {
-        size_t nv = n / 16;
-        for (size_t i = threadIdx.x; i < nv; i += blockDim.x)
-            st_v4(dst + i * 16, *reinterpret_cast<const uint4 *>(src + i * 16));
-        for (size_t e = nv * 16 / sizeof(T) + threadIdx.x; e < n / sizeof(T); e += blockDim.x)
-            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+        for (size_t i = lo / 16 + threadIdx.x; i < hi / 16; i += blockDim.x) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(src + i * 16);
+#pragma unroll
+            for (int q = 0; q < kMaxRanks; ++q)
+                if (q < P) st_v4(dst[q] + i * 16, v);
+        }
+        for (size_t e = (hi / 16) * 16 / sizeof(T) + threadIdx.x; e < hi / sizeof(T); e += blockDim.x) {
+            const T v = reinterpret_cast<const T *>(src)[e];
+            for (int q = 0; q < P; ++q) reinterpret_cast<T *>(dst[q])[e] = v;
+        }
     } else {
-        for (size_t e = threadIdx.x; e < n / sizeof(T); e += blockDim.x)
-            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+        for (size_t e = lo / sizeof(T) + threadIdx.x; e < hi / sizeof(T); e += blockDim.x) {
+            const T v = reinterpret_cast<const T *>(src)[e];
+            for (int q = 0; q < P; ++q) reinterpret_cast<T *>(dst[q])[e] = v;
+        }
     }
 }
 
-// ---------------------------------------------------------------- one-shot
 template <int OP, typename T>
 __global__ void __launch_bounds__(512) oneshot_kernel(OneShotArgs a) {
     __shared__ int s_fail;
@@ -115,11 +122,12 @@ __global__ void __launch_bounds__(512) oneshot_kernel(OneShotArgs a) {
     const size_t hi = min(min((size_t)(blockIdx.x + 1) * per, n16) * 16, bytes);
     if (threadIdx.x == 0) s_fail = 0;
 
-    // 1. copy-in of this block's share into this rank's scratch
-    if (hi > lo) block_copy<T>(a.my_scratch + lo, a.src + lo, hi - lo);
+    // 1. push this block's share of the input into every rank's slot
+    if (hi > lo) block_push<T>(a.slot_out, a.P, a.src, lo, hi);
     __syncthreads();
 
-    // 2. arrive at every peer, 3. wait for every peer
+    // 2. signal every peer (the release orders the block's stores before
+    //    the flag), 3. wait for every peer's signal
     const int t = threadIdx.x;
     if (t < a.P && t != a.rank)
         st_release_sys(a.peer_flags[t] + a.rank * kMaxBlocks + blockIdx.x, a.epoch);
@@ -134,14 +142,14 @@ __global__ void __launch_bounds__(512) oneshot_kernel(OneShotArgs a) {
     __syncthreads();
     if (s_fail) return;
 
-    // 4. reduce the share from all P scratch copies in rank order
+    // 4. fold the P local slots in rank order
     const size_t vlo = lo / 16, vhi = hi / 16;
     const bool dst_vec = ((uintptr_t)a.dst & 15) == 0;
     for (size_t i = vlo + threadIdx.x; i < vhi; i += blockDim.x) {
         uint4 v[kMaxRanks];
 #pragma unroll
         for (int q = 0; q < kMaxRanks; ++q)
-            if (q < a.P) v[q] = ld_v4(a.scratch[q] + i * 16);
+            if (q < a.P) v[q] = ld_v4(a.slot_in + (size_t)q * a.slot_bytes + i * 16);
         uint4 acc = v[0];
 #pragma unroll
         for (int q = 1; q < kMaxRanks; ++q)
@@ -157,8 +165,9 @@ __global__ void __launch_bounds__(512) oneshot_kernel(OneShotArgs a) {
     }
     // ragged end (last block only)
     for (size_t e = vhi * 16 / sizeof(T) + threadIdx.x; e < hi / sizeof(T); e += blockDim.x) {
-        T acc = reinterpret_cast<const T *>(a.scratch[0])[e];
-        for (int q = 1; q < a.P; ++q) acc = apply<OP, T>(acc, reinterpret_cast<const T *>(a.scratch[q])[e]);
+        T acc = reinterpret_cast<const T *>(a.slot_in)[e];
+        for (int q = 1; q < a.P; ++q)
+            acc = apply<OP, T>(acc, reinterpret_cast<const T *>(a.slot_in + (size_t)q * a.slot_bytes)[e]);
         reinterpret_cast<T *>(a.dst)[e] = acc;
     }
 }
@@ -179,7 +188,34 @@ __global__ void __launch_bounds__(512) twoshot_kernel(TwoShotArgs a) {
     if (a.vector_ok) {
         const size_t lo = a.nvec * a.rank / a.P, hi = a.nvec * (a.rank + 1) / a.P;
         const size_t base = a.head * sizeof(T);
-        for (size_t i = lo + tid; i < hi; i += stride) {
+        size_t i = lo + tid;
+        if (a.unroll2) {
+            // two vectors per iteration: 2P independent loads in flight
+            for (; i + stride < hi; i += 2 * stride) {
+                const size_t o0 = base + i * 16, o1 = o0 + stride * 16;
+                uint4 v0[kMaxRanks], v1[kMaxRanks];
+#pragma unroll
+                for (int q = 0; q < kMaxRanks; ++q)
+                    if (q < a.P) {
+                        v0[q] = ld_v4(a.src[q] + o0);
+                        v1[q] = ld_v4(a.src[q] + o1);
+                    }
+                uint4 acc0 = v0[0], acc1 = v1[0];
+#pragma unroll
+                for (int q = 1; q < kMaxRanks; ++q)
+                    if (q < a.P) {
+                        acc0 = vop<OP, T>(acc0, v0[q]);
+                        acc1 = vop<OP, T>(acc1, v1[q]);
+                    }
+#pragma unroll
+                for (int q = 0; q < kMaxRanks; ++q)
+                    if (q < a.P) {
+                        st_v4(a.dst[q] + o0, acc0);
+                        st_v4(a.dst[q] + o1, acc1);
+                    }
+            }
+        }
+        for (; i < hi; i += stride) {
             const size_t off = base + i * 16;
             uint4 v[kMaxRanks];
 #pragma unroll
@@ -210,7 +246,7 @@ __global__ void __launch_bounds__(512) twoshot_kernel(TwoShotArgs a) {
 // (also serves s32/s64: wrapping addition has the same bits), f32 (also as
 // .v4) and f64; min/max on u32, s32, u64, s64.  No PROD, no 8/16-bit
 // integers, no floating-point min/max: those pairs stay on the P2P kernels.
-template <int OP, int EC> struct Mm { static constexpr bool ok = false; static constexpr int bytes = 16; };
+template <int OP, int EC> struct Mm { static constexpr bool ok = false; };
 
 #define CAIL_MM_SCALAR(OPC, ECC, PTX, CT, CONS)                                                 \
     template <> struct Mm<OPC, ECC> {                                                           \

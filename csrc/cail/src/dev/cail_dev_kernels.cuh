@@ -21,15 +21,18 @@ struct DevStatus {
     unsigned int seen;
 };
 
-// One-shot: every rank copies its input into its scratch half `parity`,
-// signals every peer, waits for every peer's signal, then reduces all P
-// scratch copies (rank order) into its own output.
+// One-shot (push): every rank writes its input into slot `rank` of every
+// rank's scratch (posted NVLink stores), signals each peer with a release
+// flag per CTA, waits for the P-1 flags addressed to it, then folds its P
+// local slots in rank order into its output.  Scratch is double-buffered
+// by epoch parity, so no trailing barrier is needed.
 struct OneShotArgs {
     const char *src;                 // this rank's input (user buffer)
     char *dst;                       // this rank's output (user buffer)
-    size_t count;                    // elements
-    const char *scratch[kMaxRanks];  // each rank's scratch half for this call (peer mappings)
-    char *my_scratch;                // == scratch[rank]
+    size_t count;                    // elements (count * size <= slot bytes)
+    char *slot_out[kMaxRanks];       // slot `rank` of each rank's scratch, this parity (peer mappings)
+    const char *slot_in;             // slot 0 of this rank's scratch, this parity
+    size_t slot_bytes;               // distance between slots
     uint32_t *peer_flags[kMaxRanks]; // each rank's arrival flag array (peer mappings)
     uint32_t *my_flags;              // this rank's arrival flag array
     int P, rank;
@@ -49,6 +52,7 @@ struct TwoShotArgs {
     size_t nvec;                     // 16-byte vectors after the head
     int P, rank;
     int vector_ok;                   // all buffers share the same alignment mod 16
+    int unroll2;                     // process two vectors per loop iteration
 };
 
 // NVLS two-shot of one chunk: every rank copies its chunk into its unicast

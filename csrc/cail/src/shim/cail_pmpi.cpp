@@ -79,10 +79,7 @@ int MPI_Allreduce(const void *sendbuf, void *recvbuf, int count, MPI_Datatype da
     cail_prof_mark(CAIL_PH_FILTER, t_in);
     int may_fallback = 1;
     rc = cail_allreduce_dispatch_ex(sendbuf, recvbuf, count, datatype, op, comm, &may_fallback);
-    if (cail_global_state.profile) {
-        cail_prof_mark(CAIL_PH_TOTAL, t_in);
-        cail_prof_calls++;
-    }
+    if (cail_global_state.profile) cail_prof_end_call(cail_now_us() - t_in);
     if (rc != MPI_SUCCESS) {
         if (!may_fallback) {
             CAIL_ERR("device allreduce failed (rc=%d); not retrying through PMPI", rc);

@@ -416,8 +416,8 @@ static void queue_ack(int to, uint64_t rid) {
 
 // Completes receive r from a fully arrived unexpected message u.
 static void deliver_unexpected(Request *r, Unexpected *u) {
-    set_status(r, u->src, u->tag, u->len);
     if (u->type == PKT_EAGER) {
+        set_status(r, u->src, u->tag, u->len);
         uint64_t n = std::min<uint64_t>(u->len, r->bytes);
         if (n) {
             if (r->dev) cuda_copy(r->buf, u->data.data(), n, r->dev_ordinal);
@@ -426,6 +426,7 @@ static void deliver_unexpected(Request *r, Unexpected *u) {
     } else {
         RndvDesc d;
         memcpy(&d, u->data.data(), sizeof(d));
+        set_status(r, u->src, u->tag, d.bytes);  // the message size, not the descriptor's
         d.bytes = std::min<uint64_t>(d.bytes, r->bytes);
         int rc = d.bytes ? ipc_pull(u->src, d, r->buf, r->dev, r->dev_ordinal) : MPI_SUCCESS;
         if (rc != MPI_SUCCESS) r->err = rc;
