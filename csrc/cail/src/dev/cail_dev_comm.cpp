@@ -77,6 +77,8 @@ struct Driver {
     CUresult (*multicastAddDevice)(CUmemGenericAllocationHandle, CUdevice) = nullptr;
     CUresult (*multicastBindMem)(CUmemGenericAllocationHandle, size_t, CUmemGenericAllocationHandle,
                                  size_t, size_t, unsigned long long) = nullptr;
+    CUresult (*multicastBindAddr)(CUmemGenericAllocationHandle, size_t, CUdeviceptr, size_t,
+                                  unsigned long long) = nullptr;
     CUresult (*multicastUnbind)(CUmemGenericAllocationHandle, CUdevice, size_t, size_t) = nullptr;
     CUresult (*multicastGetGranularity)(size_t *, const CUmulticastObjectProp *,
                                         CUmulticastGranularity_flags) = nullptr;
@@ -112,6 +114,7 @@ void load_driver() {
     load_sym("cuMulticastCreate", g_drv.multicastCreate);
     load_sym("cuMulticastAddDevice", g_drv.multicastAddDevice);
     load_sym("cuMulticastBindMem", g_drv.multicastBindMem);
+    load_sym("cuMulticastBindAddr", g_drv.multicastBindAddr);
     load_sym("cuMulticastUnbind", g_drv.multicastUnbind);
     load_sym("cuMulticastGetGranularity", g_drv.multicastGetGranularity);
 }
@@ -493,6 +496,7 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     ap.type = CU_MEM_ALLOCATION_TYPE_PINNED;
     ap.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
     ap.location.id = cd;
+    ap.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;  // as the multicast object
     size_t g1 = 0, g2 = 0;
     mp.size = kNvlsCounterBytes + 2 * half;
     ok = nvls_step(dc, ok, g_drv.multicastGetGranularity(&g1, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED),
@@ -529,9 +533,6 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     ok = nvls_step(dc, ok, g_drv.multicastAddDevice(dc->mc_handle, cd), "cuMulticastAddDevice");
     if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }  // every device added before binding
     ok = nvls_step(dc, ok, g_drv.memCreate(&dc->phys_handle, size, &ap, 0), "cuMemCreate");
-    ok = nvls_step(dc, ok, g_drv.multicastBindMem(dc->mc_handle, 0, dc->phys_handle, 0, size, 0),
-                   "cuMulticastBindMem");
-    dc->mc_bound = ok;
     CUmemAccessDesc acc;
     memset(&acc, 0, sizeof(acc));
     acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
@@ -540,6 +541,15 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     ok = nvls_step(dc, ok, g_drv.memAddressReserve(&dc->uc_va, size, gran, 0, 0), "cuMemAddressReserve(uc)");
     ok = nvls_step(dc, ok, g_drv.memMap(dc->uc_va, size, 0, dc->phys_handle, 0), "cuMemMap(uc)");
     ok = nvls_step(dc, ok, g_drv.memSetAccess(dc->uc_va, size, &acc, 1), "cuMemSetAccess(uc)");
+    if (ok) {
+        CUresult r = g_drv.multicastBindMem(dc->mc_handle, 0, dc->phys_handle, 0, size, 0);
+        if (r != CUDA_SUCCESS && g_drv.multicastBindAddr) {
+            CAIL_DBG("nvls: rank %d: cuMulticastBindMem returned %d, trying cuMulticastBindAddr", dc->rank, (int)r);
+            r = g_drv.multicastBindAddr(dc->mc_handle, 0, dc->uc_va, size, 0);
+        }
+        ok = nvls_step(dc, ok, r, "cuMulticastBind");
+        dc->mc_bound = ok;
+    }
     ok = nvls_step(dc, ok, g_drv.memAddressReserve(&dc->mc_va, size, gran, 0, 0), "cuMemAddressReserve(mc)");
     ok = nvls_step(dc, ok, g_drv.memMap(dc->mc_va, size, 0, dc->mc_handle, 0), "cuMemMap(mc)");
     ok = nvls_step(dc, ok, g_drv.memSetAccess(dc->mc_va, size, &acc, 1), "cuMemSetAccess(mc)");

@@ -180,7 +180,7 @@ __device__ __forceinline__ void scalar_elem(const TwoShotArgs &a, size_t e) {
     for (int q = 0; q < a.P; ++q) reinterpret_cast<T *>(a.dst[q])[e] = acc;
 }
 
-template <int OP, typename T>
+template <int OP, typename T, bool U2>
 __global__ void __launch_bounds__(512) twoshot_kernel(TwoShotArgs a) {
     constexpr int V = 16 / sizeof(T);
     const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(512) twoshot_kernel(TwoShotArgs a) {
         const size_t lo = a.nvec * a.rank / a.P, hi = a.nvec * (a.rank + 1) / a.P;
         const size_t base = a.head * sizeof(T);
         size_t i = lo + tid;
-        if (a.unroll2) {
+        if constexpr (U2) {
             // two vectors per iteration: 2P independent loads in flight
             for (; i + stride < hi; i += 2 * stride) {
                 const size_t o0 = base + i * 16, o1 = o0 + stride * 16;
@@ -394,7 +394,10 @@ struct LaunchTwoShot {
     int b, t;
     cudaStream_t s;
     template <int OP, int EC> void operator()() {
-        twoshot_kernel<OP, typename EcType<EC>::T><<<b, t, 0, s>>>(a);
+        if (a.unroll2)
+            twoshot_kernel<OP, typename EcType<EC>::T, true><<<b, t, 0, s>>>(a);
+        else
+            twoshot_kernel<OP, typename EcType<EC>::T, false><<<b, t, 0, s>>>(a);
     }
 };
 

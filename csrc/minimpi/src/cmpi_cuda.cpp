@@ -137,6 +137,10 @@ int cuda_copy(void *dst, const void *src, uint64_t bytes, int ordinal_hint) {
 bool ipc_describe(const void *p, uint64_t bytes, int ordinal, RndvDesc *d) {
     if (!p_getattr || !p_range) return false;
     if (const char *e = getenv("CMPI_NO_IPC"); e && *e && *e != '0') return false;
+    // The receiver copies out of this buffer from its own process, outside
+    // this process' stream order: let queued legacy-stream work that may
+    // still write the buffer (e.g. the DMA of a pageable cudaMemcpy) finish.
+    with_device(ordinal, [](int) { return cudaStreamSynchronize(cudaStreamLegacy) == cudaSuccess ? 0 : 1; });
     unsigned long long id = 0;
     if (p_getattr(&id, CU_POINTER_ATTRIBUTE_BUFFER_ID, (CUdeviceptr)p) != CUDA_SUCCESS) return false;
     auto it = g_exports.find(id);
