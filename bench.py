@@ -242,24 +242,26 @@ def main() -> None:
         return cail_b200.stats().launches
 
     # ---------------- headline: K timed steps of the full message
+    # nvidia-smi samples every 100 ms from before the warm-up to the end of
+    # the sweep, a window that contains the (short) timed region
+    from cail_b200.utils import ClockSampler
+    clocks = ClockSampler(local, period_ms=100).__enter__()
+    time.sleep(0.3)
     for _ in range(args.warmup):
         allreduce(send, recv)
-    from cail_b200.utils import ClockSampler
     comm.barrier()
     torch.cuda.synchronize()
     l0 = stats_launches()
-    with ClockSampler(local) as clocks:
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(args.steps):
-            allreduce(send, recv)
-        end.record()
-        torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        allreduce(send, recv)
+    end.record()
+    torch.cuda.synchronize()
     comm.barrier()
     l1 = stats_launches()
     t_step = comm.max(start.elapsed_time(end) / 1e3 / args.steps)
     value = busbw(args.bytes, t_step, P)
-    clock_summary = clocks.summary()
     algo = None
     if args.impl == "ours":
         import cail_b200
@@ -320,6 +322,10 @@ def main() -> None:
                 row["algo"] = cail_b200.last_algorithm()
             sweep.append(row)
             nbytes *= 2
+    clocks.__exit__(None, None, None)
+    clock_summary = clocks.summary()
+    if clock_summary is not None:
+        clock_summary["window"] = "warm-up + timed region + e2e + sweep"
 
     out = {
         "metric": METRIC,

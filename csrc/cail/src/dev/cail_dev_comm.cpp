@@ -125,7 +125,7 @@ constexpr size_t kSlotBytes = 1 << 20;                  // one-shot: bytes per s
 constexpr size_t kScratchParity = kMaxRanks * kSlotBytes;  // one slot per source rank
 constexpr size_t kWorkspaceBytes = kFlagBytes + 2 * kScratchParity;
 constexpr size_t kNvlsCounterBytes = 2 << 20;           // counter page(s) of the multicast region
-constexpr size_t kDefaultNvlsHalf = 128ull << 20;       // NVLS staging per half
+constexpr size_t kDefaultNvlsSlot = 32ull << 20;        // NVLS: bytes per staging slot (3 slots)
 
 // ---------------------------------------------------------------- host exchange
 struct BufDesc {
@@ -224,13 +224,12 @@ struct cail_dev_comm {
     std::list<ImportKey> lru;
     // NVLS
     bool nvls = false;
-    size_t nvls_half = 0, nvls_size = 0;
+    size_t nvls_slot = 0, nvls_size = 0;
     CUmemGenericAllocationHandle mc_handle = 0, phys_handle = 0;
     CUdeviceptr uc_va = 0, mc_va = 0;
     bool mc_bound = false;
     uint32_t nvls_expected = 0;
     int nvls_blocks = 0;
-    int nvls_next_half = 0;
     double last_live_check = 0.0;
     cudaEvent_t legacy_ev = nullptr;  // marks the legacy stream's queue at call entry
 };
@@ -480,10 +479,10 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
         CAIL_DBG("nvls: driver entry points missing");
         return;
     }
-    size_t half = kDefaultNvlsHalf;
+    size_t slot = kDefaultNvlsSlot;
     if (const char *e = getenv("CAIL_NVLS_CHUNK")) {
         long v = atol(e);
-        if (v >= (1 << 20)) half = (size_t)v;
+        if (v >= (1 << 20)) slot = ((size_t)v + 65535) / 65536 * 65536;
     }
     CUdevice cd = 0;
     bool ok = nvls_step(dc, true, g_drv.deviceGet(&cd, dc->dev), "cuDeviceGet");
@@ -498,17 +497,17 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     ap.location.id = cd;
     ap.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;  // as the multicast object
     size_t g1 = 0, g2 = 0;
-    mp.size = kNvlsCounterBytes + 2 * half;
+    mp.size = kNvlsCounterBytes + cail::kNvlsSlots * slot;
     ok = nvls_step(dc, ok, g_drv.multicastGetGranularity(&g1, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED),
                    "cuMulticastGetGranularity");
     ok = nvls_step(dc, ok, g_drv.memGetAllocationGranularity(&g2, &ap, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED),
                    "cuMemGetAllocationGranularity");
     size_t gran = g1 > g2 ? g1 : g2;
     if (gran == 0) gran = 2 << 20;
-    size_t size = (kNvlsCounterBytes + 2 * half + gran - 1) / gran * gran;
+    size_t size = (kNvlsCounterBytes + cail::kNvlsSlots * slot + gran - 1) / gran * gran;
     mp.size = size;
     dc->nvls_size = size;
-    dc->nvls_half = half;
+    dc->nvls_slot = slot;
     if (!agree(dc->comm, ok)) return;
 
     int fd = -1;
@@ -563,7 +562,7 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     // grid-wide counter barrier of the NVLS kernel requires
     dc->nvls_blocks = dc->sms * 2;
     dc->nvls = true;
-    CAIL_DBG("nvls: multicast region of %zu bytes (granularity %zu), staging 2 x %zu", size, gran, half);
+    CAIL_DBG("nvls: multicast region of %zu bytes (granularity %zu), staging %d x %zu", size, gran, cail::kNvlsSlots, slot);
 }
 
 void destroy_context(cail_dev_comm *dc) {
@@ -833,16 +832,22 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
         size_t work = vec_ok ? a.nvec / dc->P + 1 : count / dc->P + 1;
         int threads = 512;
         size_t want = (work + threads - 1) / threads;
-        static const int per_sm = [] {
+        // Measured on 2 x B200 (1 GiB): two vectors per iteration with one
+        // 512-thread CTA per SM moves ~5% more than one vector with two CTAs
+        // per SM; below 128 MiB the plain loop is as fast or faster.
+        // CAIL_TWOSHOT_CTAS_PER_SM / CAIL_TWOSHOT_UNROLL (1 or 2) override.
+        static const int env_per_sm = [] {
             const char *e = getenv("CAIL_TWOSHOT_CTAS_PER_SM");
-            int v = e ? atoi(e) : 2;
-            return v >= 1 && v <= 4 ? v : 2;
+            int v = e ? atoi(e) : 0;
+            return v >= 1 && v <= 4 ? v : 0;
         }();
-        static const int unroll2 = [] {
+        static const int env_unroll = [] {
             const char *e = getenv("CAIL_TWOSHOT_UNROLL");
-            return e && atoi(e) >= 2 ? 1 : 0;
+            return e ? atoi(e) : 0;
         }();
-        a.unroll2 = unroll2;
+        const bool big = count * esz >= ((size_t)128 << 20);
+        a.unroll2 = env_unroll ? (env_unroll >= 2 ? 1 : 0) : (big ? 1 : 0);
+        int per_sm = env_per_sm ? env_per_sm : (a.unroll2 ? 1 : 2);
         int maxb = dc->sms * per_sm;
         int blocks = (int)(want < 1 ? 1 : (want > (size_t)maxb ? maxb : want));
         double tl = cail_global_state.profile ? cail_now_us() : 0.0;
@@ -867,39 +872,41 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
 
 // ---- NVLS
 int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec) {
-    const size_t per = dc->nvls_half / esz;
-    char *uc = (char *)dc->uc_va + kNvlsCounterBytes;
-    char *mcp = (char *)dc->mc_va + kNvlsCounterBytes;
     const int blocks = dc->nvls_blocks;
     const uint32_t step = (uint32_t)(dc->P * blocks);
-    for (size_t off = 0; off < count; off += per) {
-        size_t n = count - off < per ? count - off : per;
-        int h = dc->nvls_next_half;
-        dc->nvls_next_half ^= 1;
-        cail::NvlsArgs a;
-        memset(&a, 0, sizeof(a));
-        a.src = src + off * esz;
-        a.dst = dst + off * esz;
-        a.uc = uc + (size_t)h * dc->nvls_half;
-        a.mc = mcp + (size_t)h * dc->nvls_half;
-        a.mc_counter = (uint32_t *)dc->mc_va;
-        a.uc_counter = (const uint32_t *)dc->uc_va;
-        a.count = n;
-        a.P = dc->P;
-        a.rank = dc->rank;
-        dc->nvls_expected += step;
-        a.target_a = dc->nvls_expected;
-        dc->nvls_expected += step;
-        a.target_b = dc->nvls_expected;
-        a.timeout_ns = timeout_ns();
-        a.status = dc->status_d;
-        cudaError_t e = cail::launch_nvls(op, ec, a, blocks, 512, dc->stream);
-        cail_counters.launches++;
-        if (e != cudaSuccess) {
-            CAIL_ERR("nvls launch failed: %s", cudaGetErrorString(e));
-            dc->broken = true;
-            return MPI_ERR_OTHER;
-        }
+    // Sub-chunk: a quarter of the message (so small messages still overlap
+    // their stages), between 2 MiB and one staging slot, in 64 KiB units.
+    size_t sub_bytes = count * esz / 4;
+    sub_bytes = sub_bytes < ((size_t)2 << 20) ? ((size_t)2 << 20) : sub_bytes;
+    sub_bytes = (sub_bytes + 65535) / 65536 * 65536;
+    if (sub_bytes > dc->nvls_slot) sub_bytes = dc->nvls_slot;
+    cail::NvlsArgs a;
+    memset(&a, 0, sizeof(a));
+    a.src = src;
+    a.dst = dst;
+    a.uc = (char *)dc->uc_va + kNvlsCounterBytes;
+    a.mc = (char *)dc->mc_va + kNvlsCounterBytes;
+    a.mc_counter = (uint32_t *)dc->mc_va;
+    a.uc_counter = (const uint32_t *)dc->uc_va;
+    a.count = count;
+    a.sub = sub_bytes / esz;
+    a.slot_bytes = dc->nvls_slot;
+    a.P = dc->P;
+    a.rank = dc->rank;
+    a.target0 = dc->nvls_expected;
+    a.step = step;
+    a.timeout_ns = timeout_ns();
+    a.status = dc->status_d;
+    const size_t nsub = (count + a.sub - 1) / a.sub;
+    dc->nvls_expected += (uint32_t)(nsub + 2) * step;  // one barrier per pipeline iteration
+    double t = cail_global_state.profile ? cail_now_us() : 0.0;
+    cudaError_t e = cail::launch_nvls(op, ec, a, blocks, 512, dc->stream);
+    cail_prof_mark(CAIL_PH_LAUNCH, t);
+    cail_counters.launches++;
+    if (e != cudaSuccess) {
+        CAIL_ERR("nvls launch failed: %s", cudaGetErrorString(e));
+        dc->broken = true;
+        return MPI_ERR_OTHER;
     }
     return check_status(dc, "nvls");
 }
@@ -910,9 +917,25 @@ size_t default_oneshot_max(int P) {
     return 512 << 10;
 }
 
+// NVLS moves about N(1 + 1/P) bytes per GPU and direction plus a local
+// copy-in and copy-out, against 2N(P-1)/P for two-shot: it can only win at
+// large P.  Measured on 2 x B200 it reaches 44% of two-shot, so auto mode
+// uses it from CAIL_NVLS_MIN_RANKS ranks (default 8) and CAIL_NVLS_MIN
+// bytes (default 16 MiB).
 size_t nvls_min_bytes() {
-    if (const char *e = getenv("CAIL_NVLS_MIN")) return (size_t)atoll(e);
-    return 4 << 20;
+    static const size_t v = [] {
+        const char *e = getenv("CAIL_NVLS_MIN");
+        return e ? (size_t)atoll(e) : (size_t)16 << 20;
+    }();
+    return v;
+}
+
+int nvls_min_ranks() {
+    static const int v = [] {
+        const char *e = getenv("CAIL_NVLS_MIN_RANKS");
+        return e ? atoi(e) : 8;
+    }();
+    return v;
 }
 
 }  // namespace
@@ -948,7 +971,8 @@ int cail_dev_pick_algo(cail_dev_comm *dc, size_t bytes, int count, cail_datatype
                                    : (s.msg_small_threshold_set ? s.msg_small_threshold - 1
                                                                 : default_oneshot_max(dc->P));
     if (bytes <= one_max) return CAIL_ALGO_ONE_SHOT;
-    if (cail_dev_nvls_ok(dc, dt, op) && bytes >= nvls_min_bytes()) return CAIL_ALGO_NVLS;
+    if (dc->P >= nvls_min_ranks() && cail_dev_nvls_ok(dc, dt, op) && bytes >= nvls_min_bytes())
+        return CAIL_ALGO_NVLS;
     return CAIL_ALGO_TWO_SHOT;
 }
 

@@ -322,37 +322,45 @@ __device__ __forceinline__ void grid_copy(char *dst, const char *src, size_t n) 
     }
 }
 
+// Two CTAs of 512 threads per SM must be co-resident (the barrier is grid
+// wide), hence the register cap of __launch_bounds__(512, 2).
 template <int OP, int EC>
-__global__ void __launch_bounds__(512) nvls_kernel(NvlsArgs a) {
+__global__ void __launch_bounds__(512, 2) nvls_kernel(NvlsArgs a) {
     using T = typename EcType<EC>::T;
     using M = Mm<OP, EC>;
     __shared__ int s_fail;
     if (threadIdx.x == 0) s_fail = 0;
-    const size_t bytes = a.count * sizeof(T);
-
-    grid_copy<T>(a.uc, a.src, bytes);  // copy-in
-    fence_proxy_alias();
-    __syncthreads();
-    if (threadIdx.x == 0 && !nvls_barrier(a, a.target_a, 0)) s_fail = 1;
-    __syncthreads();
-    if (s_fail) return;
-    fence_proxy_alias();
-
-    // this rank's slice of multimem units (the last unit may run past
-    // `count` into the staging padding; only `bytes` are copied out)
-    const size_t units = (bytes + M::bytes - 1) / M::bytes;
-    const size_t lo = units * a.rank / a.P, hi = units * (a.rank + 1) / a.P;
+    const size_t nsub = (a.count + a.sub - 1) / a.sub;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
-    for (size_t u = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; u < hi; u += stride)
-        M::run(a.mc + u * M::bytes);
-    fence_proxy_alias();
-    __syncthreads();
-    if (threadIdx.x == 0 && !nvls_barrier(a, a.target_b, 1)) s_fail = 1;
-    __syncthreads();
-    if (s_fail) return;
-    fence_proxy_alias();
+    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    auto sub_elems = [&](size_t j) { return min(a.sub, a.count - j * a.sub); };
 
-    grid_copy<T>(a.dst, a.uc, bytes);  // copy-out
+    for (size_t k = 0; k < nsub + 2; ++k) {
+        if (k < nsub) {  // copy-in of sub-chunk k
+            grid_copy<T>(a.uc + (k % kNvlsSlots) * a.slot_bytes, a.src + k * a.sub * sizeof(T),
+                         sub_elems(k) * sizeof(T));
+        }
+        if (k >= 1 && k <= nsub) {  // reduce + broadcast this rank's slice of sub-chunk k-1
+            const size_t j = k - 1;
+            // the last unit may run past the data into the slot's padding;
+            // only real bytes are copied out
+            const size_t units = (sub_elems(j) * sizeof(T) + M::bytes - 1) / M::bytes;
+            const size_t lo = units * a.rank / a.P, hi = units * (a.rank + 1) / a.P;
+            char *mc = a.mc + (j % kNvlsSlots) * a.slot_bytes;
+            for (size_t u = lo + tid; u < hi; u += stride) M::run(mc + u * M::bytes);
+        }
+        if (k >= 2) {  // copy-out of sub-chunk k-2
+            const size_t j = k - 2;
+            grid_copy<T>(a.dst + j * a.sub * sizeof(T), a.uc + (j % kNvlsSlots) * a.slot_bytes,
+                         sub_elems(j) * sizeof(T));
+        }
+        fence_proxy_alias();
+        __syncthreads();
+        if (threadIdx.x == 0 && !nvls_barrier(a, a.target0 + (uint32_t)(k + 1) * a.step, (int)k)) s_fail = 1;
+        __syncthreads();
+        if (s_fail) return;
+        fence_proxy_alias();
+    }
 }
 
 // ---------------------------------------------------------------- local reduce

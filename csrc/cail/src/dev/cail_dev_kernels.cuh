@@ -55,23 +55,30 @@ struct TwoShotArgs {
     int unroll2;                     // process two vectors per loop iteration
 };
 
-// NVLS two-shot of one chunk: every rank copies its chunk into its unicast
-// view of a multicast-bound staging buffer; after a barrier rank r reduces
-// its slice with multimem.ld_reduce through the multicast view and
-// broadcasts it with multimem.st; after a second barrier every rank copies
-// the chunk out.  The barrier is a counter in the multicast region that each
-// CTA of each rank increments once (multimem.red); a barrier is passed when
-// the local copy of the counter reaches its target.
+// Pipelined NVLS allreduce of a whole message.  The message is cut into
+// sub-chunks that flow through a ring of 3 staging slots in a
+// multicast-bound region.  Iteration k (k = 0 .. K+1) copies sub-chunk k into
+// this rank's slot k%3, reduces this rank's slice of sub-chunk k-1 with
+// multimem.ld_reduce through the multicast view and broadcasts it with
+// multimem.st, and copies sub-chunk k-2 out of its slot; then all CTAs of
+// all ranks meet at a barrier.  With 3 slots, every slot's previous readers
+// and writers are done before the barrier that precedes its reuse.  The
+// barrier is a counter in the multicast region that each CTA of each rank
+// increments once per iteration (multimem.red); iteration k is complete
+// when the local copy reaches target0 + (k + 1) * step.
+constexpr int kNvlsSlots = 3;
 struct NvlsArgs {
-    const char *src;                 // this rank's input chunk (user buffer)
-    char *dst;                       // this rank's output chunk (user buffer)
-    char *uc;                        // unicast view of this chunk's staging half
-    char *mc;                        // multicast view of the same staging half
+    const char *src;                 // this rank's input (user buffer)
+    char *dst;                       // this rank's output (user buffer)
+    char *uc;                        // unicast view of slot 0 (slots are slot_bytes apart)
+    char *mc;                        // multicast view of slot 0
     uint32_t *mc_counter;            // multicast view of the barrier counter
     const uint32_t *uc_counter;      // this rank's unicast view of the counter
-    size_t count;                    // elements in this chunk
+    size_t count;                    // elements in the message
+    size_t sub;                      // elements per sub-chunk (sub * size is a multiple of 16)
+    size_t slot_bytes;
     int P, rank;
-    uint32_t target_a, target_b;     // counter values that complete barrier A / B
+    uint32_t target0, step;
     unsigned long long timeout_ns;
     DevStatus *status;
 };

@@ -91,7 +91,11 @@ def test_reference_sm100a_build_runs_on_device_buffers():
 
 # ---------------------------------------------------------------- NVLink kernels
 def nranks():
-    return [n for n in (2, 4, 8) if n <= gpu_count()]
+    """Rank counts for the NVLink tests: 2, 4, 8 (those the box has GPUs for),
+    or the comma-separated list in CAIL_TEST_NRANKS."""
+    want = os.environ.get("CAIL_TEST_NRANKS")
+    cand = [int(x) for x in want.split(",")] if want else [2, 4, 8]
+    return [n for n in cand if n <= gpu_count()]
 
 
 @pytest.mark.multigpu
