@@ -207,13 +207,16 @@ def main() -> None:
         impl = {"ours": "ours", "reference": "reference", "pmpi": "none"}[args.impl]
         cail_b200.init(impl)
         comm = Comm(args.impl, cail_b200.rank(), cail_b200.world_size())
-        libs = _lib.loaded()
         H = _lib.H
-        import ctypes
+        from cail_b200.ops import ext
+
+        # MPI_Allreduce of the loaded library (ours or the reference) through
+        # the cail_torch extension: one pybind call, GIL released
+        ar = ext.get().allreduce
+        dt, op, cw = H["MPI_FLOAT"], H["MPI_SUM"], H["MPI_COMM_WORLD"]
 
         def allreduce(src, dst):
-            rc = libs.cail.MPI_Allreduce(ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(dst.data_ptr()),
-                                         src.numel(), H["MPI_FLOAT"], H["MPI_SUM"], H["MPI_COMM_WORLD"])
+            rc = ar(src, dst, dt, op, cw)
             if rc != 0:
                 raise RuntimeError(f"MPI_Allreduce returned {rc}")
 

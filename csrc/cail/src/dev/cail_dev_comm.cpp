@@ -228,7 +228,8 @@ struct cail_dev_comm {
     CUmemGenericAllocationHandle mc_handle = 0, phys_handle = 0;
     CUdeviceptr uc_va = 0, mc_va = 0;
     bool mc_bound = false;
-    uint32_t nvls_expected = 0;
+    uint32_t nvls_expected = 0;        // multicast counter value after the last call
+    uint32_t nvls_local_expected = 0;  // local arrival counter value after the last call
     int nvls_blocks = 0;
     double last_live_check = 0.0;
     cudaEvent_t legacy_ev = nullptr;  // marks the legacy stream's queue at call entry
@@ -873,7 +874,11 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
 // ---- NVLS
 int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec) {
     const int blocks = dc->nvls_blocks;
-    const uint32_t step = (uint32_t)(dc->P * blocks);
+    static const int copy_pct = [] {
+        const char *e = getenv("CAIL_NVLS_COPY_PCT");
+        int v = e ? atoi(e) : 50;
+        return v >= 10 && v <= 90 ? v : 50;
+    }();
     // Sub-chunk: a quarter of the message (so small messages still overlap
     // their stages), between 2 MiB and one staging slot, in 64 KiB units.
     size_t sub_bytes = count * esz / 4;
@@ -888,17 +893,21 @@ int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
     a.mc = (char *)dc->mc_va + kNvlsCounterBytes;
     a.mc_counter = (uint32_t *)dc->mc_va;
     a.uc_counter = (const uint32_t *)dc->uc_va;
+    a.local_counter = (uint32_t *)((char *)dc->uc_va + 256);  // never written through the multicast view
     a.count = count;
     a.sub = sub_bytes / esz;
     a.slot_bytes = dc->nvls_slot;
     a.P = dc->P;
     a.rank = dc->rank;
+    a.copy_blocks = blocks * copy_pct / 100;
     a.target0 = dc->nvls_expected;
-    a.step = step;
+    a.local0 = dc->nvls_local_expected;
     a.timeout_ns = timeout_ns();
     a.status = dc->status_d;
     const size_t nsub = (count + a.sub - 1) / a.sub;
-    dc->nvls_expected += (uint32_t)(nsub + 2) * step;  // one barrier per pipeline iteration
+    // one barrier per pipeline iteration: P cross-rank arrivals, `blocks` local ones
+    dc->nvls_expected += (uint32_t)(nsub + 2) * (uint32_t)dc->P;
+    dc->nvls_local_expected += (uint32_t)(nsub + 2) * (uint32_t)blocks;
     double t = cail_global_state.profile ? cail_now_us() : 0.0;
     cudaError_t e = cail::launch_nvls(op, ec, a, blocks, 512, dc->stream);
     cail_prof_mark(CAIL_PH_LAUNCH, t);

@@ -238,7 +238,11 @@ __global__ void __launch_bounds__(512) twoshot_kernel(TwoShotArgs a) {
         const size_t lo = a.count * a.rank / a.P, hi = a.count * (a.rank + 1) / a.P;
         for (size_t e = lo + tid; e < hi; e += stride) scalar_elem<OP, T>(a, e);
     }
-    __threadfence_system();
+    // Make the block's peer stores visible system-wide before the kernel
+    // retires (the host barrier that follows lets peers read them): one
+    // fence per block after the block barrier covers every thread's stores.
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
 }
 
 // ---------------------------------------------------------------- NVLS
@@ -248,14 +252,21 @@ __global__ void __launch_bounds__(512) twoshot_kernel(TwoShotArgs a) {
 // integers, no floating-point min/max: those pairs stay on the P2P kernels.
 template <int OP, int EC> struct Mm { static constexpr bool ok = false; };
 
+// Each supported pair provides V (the value of one multimem unit), ld (the
+// reduction of one unit over all GPUs, through the multicast address) and st
+// (its broadcast to all GPUs).
 #define CAIL_MM_SCALAR(OPC, ECC, PTX, CT, CONS)                                                 \
     template <> struct Mm<OPC, ECC> {                                                           \
         static constexpr bool ok = true;                                                        \
         static constexpr int bytes = sizeof(CT);                                                \
-        static __device__ __forceinline__ void run(char *mc) {                                  \
+        using V = CT;                                                                           \
+        static __device__ __forceinline__ V ld(const char *mc) {                                \
             CT v;                                                                               \
             asm volatile("multimem.ld_reduce.relaxed.sys.global." PTX " %0, [%1];"             \
                          : "=" CONS(v) : "l"(mc) : "memory");                                   \
+            return v;                                                                           \
+        }                                                                                       \
+        static __device__ __forceinline__ void st(char *mc, V v) {                              \
             asm volatile("multimem.st.relaxed.sys.global." PTX_ST_##ECC " [%0], %1;"           \
                          ::"l"(mc), CONS(v) : "memory");                                        \
         }                                                                                       \
@@ -281,29 +292,67 @@ CAIL_MM_SCALAR(CAIL_MIN, CAIL_EC_I64, "min.s64", unsigned long long, "l")
 template <> struct Mm<CAIL_SUM, CAIL_EC_F32> {
     static constexpr bool ok = true;
     static constexpr int bytes = 16;
-    static __device__ __forceinline__ void run(char *mc) {
-        float a, b, c, d;
+    using V = float4;
+    static __device__ __forceinline__ V ld(const char *mc) {
+        V v;
         asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
-                     : "=f"(a), "=f"(b), "=f"(c), "=f"(d) : "l"(mc) : "memory");
+                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(mc) : "memory");
+        return v;
+    }
+    static __device__ __forceinline__ void st(char *mc, V v) {
         asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};"
-                     ::"l"(mc), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+                     ::"l"(mc), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
     }
 };
 
 __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
-// Cross-rank + grid-wide barrier: one multimem.red per CTA, then wait for the
-// local counter.  Called by thread 0 only.
-__device__ __forceinline__ bool nvls_barrier(const NvlsArgs &a, uint32_t target, int which) {
-    asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.mc_counter), "r"(1u)
-                 : "memory");
+// Grid-wide + cross-rank barrier of pipeline iteration k, called by thread 0
+// of every CTA after a block barrier.  Two levels, so the multicast counter
+// takes one atomic per rank instead of one per CTA:
+//   1. fence, then arrive on this GPU's local counter; the CTA that arrives
+//      last (all gridDim.x arrivals of this iteration seen) fences again and
+//      adds 1 to the multicast counter on every GPU with one multimem.red;
+//   2. every CTA waits until its GPU's copy of the multicast counter shows
+//      the arrival of all P ranks.
+// The fence / atomic / fence chain orders every CTA's stores before the
+// release of the multimem.red.
+__device__ __forceinline__ bool nvls_barrier(const NvlsArgs &a, size_t k) {
+    __threadfence();
+    const uint32_t old = atomicAdd(a.local_counter, 1u);
+    if (old + 1u == a.local0 + (uint32_t)(k + 1) * gridDim.x) {
+        __threadfence();
+        fence_proxy_alias();
+        asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.mc_counter), "r"(1u)
+                     : "memory");
+    }
+    const uint32_t target = a.target0 + (uint32_t)(k + 1) * (uint32_t)a.P;
     uint32_t seen = 0;
     unsigned long long deadline = globaltimer() + a.timeout_ns;
     if (!wait_flag(a.uc_counter, target, deadline, &seen)) {
-        report(a.status, a.rank, -1 - which, blockIdx.x, target, seen);
+        report(a.status, a.rank, -1 - (int)k, blockIdx.x, target, seen);
         return false;
     }
     return true;
+}
+
+// Copies n bytes with the threads [part_tid, part_tid + part_threads) of the
+// grid; 16-byte vectors when both ends are aligned.
+template <typename T>
+__device__ __forceinline__ void part_copy(char *dst, const char *src, size_t n, size_t part_tid,
+                                          size_t part_threads) {
+    const size_t stride = part_threads;
+    const size_t tid = part_tid;
+    if ((((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
+        const size_t nv = n / 16;
+        for (size_t i = tid; i < nv; i += stride)
+            st_v4(dst + i * 16, *reinterpret_cast<const uint4 *>(src + i * 16));
+        for (size_t e = nv * 16 / sizeof(T) + tid; e < n / sizeof(T); e += stride)
+            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+    } else {
+        for (size_t e = tid; e < n / sizeof(T); e += stride)
+            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+    }
 }
 
 template <typename T>
@@ -331,32 +380,47 @@ __global__ void __launch_bounds__(512, 2) nvls_kernel(NvlsArgs a) {
     __shared__ int s_fail;
     if (threadIdx.x == 0) s_fail = 0;
     const size_t nsub = (a.count + a.sub - 1) / a.sub;
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     auto sub_elems = [&](size_t j) { return min(a.sub, a.count - j * a.sub); };
+    // Roles: the first copy_blocks CTAs move data between the user buffers
+    // and the staging slots (HBM), the others run the multimem reduction
+    // (NVLink), so both kinds of traffic are in flight at the same time.
+    const bool copier = (int)blockIdx.x < a.copy_blocks;
+    const size_t ctid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t cthreads = (size_t)a.copy_blocks * blockDim.x;
+    const size_t rtid = (size_t)(blockIdx.x - a.copy_blocks) * blockDim.x + threadIdx.x;
+    const size_t rthreads = (size_t)(gridDim.x - a.copy_blocks) * blockDim.x;
+    constexpr int U = 4;  // multimem units in flight per thread
 
     for (size_t k = 0; k < nsub + 2; ++k) {
-        if (k < nsub) {  // copy-in of sub-chunk k
-            grid_copy<T>(a.uc + (k % kNvlsSlots) * a.slot_bytes, a.src + k * a.sub * sizeof(T),
-                         sub_elems(k) * sizeof(T));
-        }
-        if (k >= 1 && k <= nsub) {  // reduce + broadcast this rank's slice of sub-chunk k-1
+        if (copier) {
+            if (k < nsub)  // copy-in of sub-chunk k
+                part_copy<T>(a.uc + (k % kNvlsSlots) * a.slot_bytes, a.src + k * a.sub * sizeof(T),
+                             sub_elems(k) * sizeof(T), ctid, cthreads);
+            if (k >= 2) {  // copy-out of sub-chunk k-2
+                const size_t j = k - 2;
+                part_copy<T>(a.dst + j * a.sub * sizeof(T), a.uc + (j % kNvlsSlots) * a.slot_bytes,
+                             sub_elems(j) * sizeof(T), ctid, cthreads);
+            }
+        } else if (k >= 1 && k <= nsub) {  // reduce + broadcast this rank's slice of sub-chunk k-1
             const size_t j = k - 1;
             // the last unit may run past the data into the slot's padding;
             // only real bytes are copied out
             const size_t units = (sub_elems(j) * sizeof(T) + M::bytes - 1) / M::bytes;
             const size_t lo = units * a.rank / a.P, hi = units * (a.rank + 1) / a.P;
             char *mc = a.mc + (j % kNvlsSlots) * a.slot_bytes;
-            for (size_t u = lo + tid; u < hi; u += stride) M::run(mc + u * M::bytes);
-        }
-        if (k >= 2) {  // copy-out of sub-chunk k-2
-            const size_t j = k - 2;
-            grid_copy<T>(a.dst + j * a.sub * sizeof(T), a.uc + (j % kNvlsSlots) * a.slot_bytes,
-                         sub_elems(j) * sizeof(T));
+            for (size_t u = lo + rtid; u < hi; u += U * rthreads) {
+                typename M::V v[U];
+#pragma unroll
+                for (int q = 0; q < U; ++q)
+                    if (u + q * rthreads < hi) v[q] = M::ld(mc + (u + q * rthreads) * M::bytes);
+#pragma unroll
+                for (int q = 0; q < U; ++q)
+                    if (u + q * rthreads < hi) M::st(mc + (u + q * rthreads) * M::bytes, v[q]);
+            }
         }
         fence_proxy_alias();
         __syncthreads();
-        if (threadIdx.x == 0 && !nvls_barrier(a, a.target0 + (uint32_t)(k + 1) * a.step, (int)k)) s_fail = 1;
+        if (threadIdx.x == 0 && !nvls_barrier(a, k)) s_fail = 1;
         __syncthreads();
         if (s_fail) return;
         fence_proxy_alias();

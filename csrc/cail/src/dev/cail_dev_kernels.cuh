@@ -63,22 +63,26 @@ struct TwoShotArgs {
 // multimem.st, and copies sub-chunk k-2 out of its slot; then all CTAs of
 // all ranks meet at a barrier.  With 3 slots, every slot's previous readers
 // and writers are done before the barrier that precedes its reuse.  The
-// barrier is a counter in the multicast region that each CTA of each rank
-// increments once per iteration (multimem.red); iteration k is complete
-// when the local copy reaches target0 + (k + 1) * step.
+// barrier has two levels: CTAs arrive on a counter local to their GPU
+// (complete at local0 + (k + 1) * gridDim.x); the last arrival adds 1 to a
+// counter in the multicast region on every GPU (multimem.red); iteration k
+// is complete when the local copy of that counter reaches
+// target0 + (k + 1) * P.  Copy work and multimem work run on disjoint CTAs.
 constexpr int kNvlsSlots = 3;
 struct NvlsArgs {
     const char *src;                 // this rank's input (user buffer)
     char *dst;                       // this rank's output (user buffer)
     char *uc;                        // unicast view of slot 0 (slots are slot_bytes apart)
     char *mc;                        // multicast view of slot 0
-    uint32_t *mc_counter;            // multicast view of the barrier counter
-    const uint32_t *uc_counter;      // this rank's unicast view of the counter
+    uint32_t *mc_counter;            // multicast view of the cross-rank counter
+    const uint32_t *uc_counter;      // this rank's unicast view of that counter
+    uint32_t *local_counter;         // this GPU's arrival counter (unicast only)
     size_t count;                    // elements in the message
     size_t sub;                      // elements per sub-chunk (sub * size is a multiple of 16)
     size_t slot_bytes;
     int P, rank;
-    uint32_t target0, step;
+    int copy_blocks;                 // CTAs [0, copy_blocks) copy, the rest reduce
+    uint32_t target0, local0;
     unsigned long long timeout_ns;
     DevStatus *status;
 };
