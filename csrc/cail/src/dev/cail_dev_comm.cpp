@@ -125,7 +125,7 @@ constexpr size_t kSlotBytes = 1 << 20;                  // one-shot: bytes per s
 constexpr size_t kScratchParity = kMaxRanks * kSlotBytes;  // one slot per source rank
 constexpr size_t kWorkspaceBytes = kFlagBytes + 2 * kScratchParity;
 constexpr size_t kNvlsCounterBytes = 2 << 20;           // counter page(s) of the multicast region
-constexpr size_t kDefaultNvlsSlot = 32ull << 20;        // NVLS: bytes per staging slot (3 slots)
+constexpr size_t kDefaultNvlsSlot = 128ull << 20;       // NVLS: bytes per staging slot (3 slots)
 
 // ---------------------------------------------------------------- host exchange
 struct BufDesc {
@@ -471,7 +471,10 @@ bool nvls_step(cail_dev_comm *dc, bool ok, CUresult r, const char *what) {
 }
 
 void nvls_setup(cail_dev_comm *dc, bool all_capable) {
-    if (!cail_global_state.nvls || dc->P < 2) return;
+    // A one-GPU multicast object is allowed only on request
+    // (CAIL_NVLS_SINGLE=1): it lets a profiler see the NVLS kernel on one GPU.
+    const char *single = getenv("CAIL_NVLS_SINGLE");
+    if (!cail_global_state.nvls || (dc->P < 2 && !(single && single[0] == '1'))) return;
     if (!all_capable) {
         CAIL_DBG("nvls: not every GPU reports CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED");
         return;
@@ -879,10 +882,17 @@ int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
         int v = e ? atoi(e) : 50;
         return v >= 10 && v <= 90 ? v : 50;
     }();
-    // Sub-chunk: a quarter of the message (so small messages still overlap
-    // their stages), between 2 MiB and one staging slot, in 64 KiB units.
-    size_t sub_bytes = count * esz / 4;
-    sub_bytes = sub_bytes < ((size_t)2 << 20) ? ((size_t)2 << 20) : sub_bytes;
+    // Sub-chunk: an eighth of the message (every pipeline stage costs one
+    // multicast barrier of tens of microseconds, so stages stay few while
+    // copies still overlap), between 4 MiB and one staging slot, in 64 KiB
+    // units.  CAIL_NVLS_STAGES overrides the eighth.
+    static const size_t stages = [] {
+        const char *e = getenv("CAIL_NVLS_STAGES");
+        long v = e ? atol(e) : 8;
+        return (size_t)(v >= 1 && v <= 1024 ? v : 8);
+    }();
+    size_t sub_bytes = count * esz / stages;
+    sub_bytes = sub_bytes < ((size_t)4 << 20) ? ((size_t)4 << 20) : sub_bytes;
     sub_bytes = (sub_bytes + 65535) / 65536 * 65536;
     if (sub_bytes > dc->nvls_slot) sub_bytes = dc->nvls_slot;
     cail::NvlsArgs a;
