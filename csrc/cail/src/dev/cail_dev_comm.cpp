@@ -471,10 +471,8 @@ bool nvls_step(cail_dev_comm *dc, bool ok, CUresult r, const char *what) {
 }
 
 void nvls_setup(cail_dev_comm *dc, bool all_capable) {
-    // A one-GPU multicast object is allowed only on request
-    // (CAIL_NVLS_SINGLE=1): it lets a profiler see the NVLS kernel on one GPU.
-    const char *single = getenv("CAIL_NVLS_SINGLE");
-    if (!cail_global_state.nvls || (dc->P < 2 && !(single && single[0] == '1'))) return;
+    // (cuMulticastCreate refuses a one-device object: INVALID_VALUE on B200)
+    if (!cail_global_state.nvls || dc->P < 2) return;
     if (!all_capable) {
         CAIL_DBG("nvls: not every GPU reports CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED");
         return;
