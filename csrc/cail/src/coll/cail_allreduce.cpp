@@ -111,7 +111,7 @@ extern "C" int cail_allreduce_dispatch_ex(const void *sendbuf, void *recvbuf, in
     // ---- NVLink device path
 #ifndef CAIL_HOST_PATH
     struct cail_dev_comm *dc = cail_dev_comm_get(comm);
-    if (forced == CAIL_ALGO_ONE_SHOT || forced == CAIL_ALGO_TWO_SHOT || forced == CAIL_ALGO_NVLS) {
+    if (cail_algo_is_device(forced)) {
         if (!dc) {
             CAIL_WARN("forced %s but the communicator has no NVLink path, falling back to PMPI",
                       cail_algo_name(forced));
@@ -142,7 +142,7 @@ extern "C" int cail_allreduce_dispatch_ex(const void *sendbuf, void *recvbuf, in
         return rc;
     }
 #else
-    if (forced == CAIL_ALGO_ONE_SHOT || forced == CAIL_ALGO_TWO_SHOT || forced == CAIL_ALGO_NVLS) {
+    if (cail_algo_is_device(forced)) {
         CAIL_WARN("forced %s needs the CUDA build, falling back to PMPI", cail_algo_name(forced));
         cail_last_algo = -3;
         cail_counters.passthrough++;

@@ -131,6 +131,7 @@ int cail_init(MPI_Comm comm) {
             {"one_shot", CAIL_ALGO_ONE_SHOT},
             {"two_shot", CAIL_ALGO_TWO_SHOT},
             {"nvls", CAIL_ALGO_NVLS},
+            {"ce_two_shot", CAIL_ALGO_CE_TWO_SHOT},
         };
         bool found = false;
         for (auto &n : names)
@@ -175,10 +176,10 @@ void cail_finalize(void) {
         const cail_stats_t &c = cail_counters;
         fprintf(stderr,
                 "[cail] stats: calls=%llu passthrough=%llu rd=%llu ring=%llu rab=%llu "
-                "one_shot=%llu two_shot=%llu nvls=%llu bytes=%llu reg_hits=%llu reg_misses=%llu "
+                "one_shot=%llu two_shot=%llu nvls=%llu ce_two_shot=%llu bytes=%llu reg_hits=%llu reg_misses=%llu "
                 "device_errors=%llu\n",
                 c.calls, c.passthrough, c.by_algo[1], c.by_algo[2], c.by_algo[3], c.by_algo[4],
-                c.by_algo[5], c.by_algo[6], c.bytes, c.reg_hits, c.reg_misses, c.device_errors);
+                c.by_algo[5], c.by_algo[6], c.by_algo[7], c.bytes, c.reg_hits, c.reg_misses, c.device_errors);
     }
     if (s.profile && cail_prof_calls) {
         const double n = (double)cail_prof_calls;

@@ -41,7 +41,7 @@ typedef enum {
 } cail_op_t;
 
 /* Algorithms.  The first three are the reference's (host-driven, over PMPI
- * point-to-point); the last three are cail-b200's NVLink kernels. */
+ * point-to-point); the others are cail-b200's NVLink paths. */
 typedef enum {
     CAIL_ALGO_AUTO = -1,
     CAIL_ALGO_RECURSIVE_DOUBLING = 0,
@@ -50,7 +50,8 @@ typedef enum {
     CAIL_ALGO_ONE_SHOT = 3,
     CAIL_ALGO_TWO_SHOT = 4,
     CAIL_ALGO_NVLS = 5,
-    CAIL_NUM_ALGOS = 6
+    CAIL_ALGO_CE_TWO_SHOT = 6,
+    CAIL_NUM_ALGOS = 7
 } cail_algo_t;
 
 /* Storage classes the kernels are instantiated for. */
@@ -58,6 +59,12 @@ typedef enum {
     CAIL_EC_I8 = 0, CAIL_EC_U8, CAIL_EC_I16, CAIL_EC_U16, CAIL_EC_I32, CAIL_EC_U32,
     CAIL_EC_I64, CAIL_EC_U64, CAIL_EC_F32, CAIL_EC_F64, CAIL_EC_NUM
 } cail_elem_class_t;
+
+/* 1 for the algorithms that run on the NVLink device path. */
+static inline int cail_algo_is_device(int a) {
+    return a == CAIL_ALGO_ONE_SHOT || a == CAIL_ALGO_TWO_SHOT || a == CAIL_ALGO_NVLS ||
+           a == CAIL_ALGO_CE_TWO_SHOT;
+}
 
 cail_datatype_t cail_mpi_type_to_dtype(MPI_Datatype dt);
 cail_op_t cail_mpi_op_to_optype(MPI_Op op);

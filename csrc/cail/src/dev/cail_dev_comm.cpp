@@ -233,6 +233,12 @@ struct cail_dev_comm {
     int nvls_blocks = 0;
     double last_live_check = 0.0;
     cudaEvent_t legacy_ev = nullptr;  // marks the legacy stream's queue at call entry
+    // copy-engine two-shot: pull / fold / push streams, per-buffer events and
+    // a scratch of kCeMaxBufs x (P-1) chunks (created on first use)
+    cudaStream_t ce_pull = nullptr, ce_fold = nullptr, ce_push = nullptr;
+    cudaEvent_t ce_pulled[4] = {}, ce_folded[4] = {}, ce_start = nullptr, ce_end = nullptr;
+    char *ce_scratch = nullptr;
+    size_t ce_scratch_bytes = 0;
 };
 
 namespace {
@@ -470,9 +476,18 @@ bool nvls_step(cail_dev_comm *dc, bool ok, CUresult r, const char *what) {
     return ok;
 }
 
+int nvls_min_ranks();
+
+// The multicast region (a 512 MiB granule per GPU) is created only where it
+// can be used: CAIL_ALGO=nvls, or auto mode with CAIL_NVLS_MIN_RANKS <= P.
+bool nvls_wanted(int P) {
+    if (!cail_global_state.nvls || P < 2) return false;
+    return cail_global_state.force_algo == CAIL_ALGO_NVLS || (nvls_min_ranks() > 0 && P >= nvls_min_ranks());
+}
+
 void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     // (cuMulticastCreate refuses a one-device object: INVALID_VALUE on B200)
-    if (!cail_global_state.nvls || dc->P < 2) return;
+    if (!nvls_wanted(dc->P)) return;
     if (!all_capable) {
         CAIL_DBG("nvls: not every GPU reports CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED");
         return;
@@ -567,6 +582,22 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     CAIL_DBG("nvls: multicast region of %zu bytes (granularity %zu), staging %d x %zu", size, gran, cail::kNvlsSlots, slot);
 }
 
+void ce_teardown(cail_dev_comm *dc) {
+    for (cudaStream_t *s : {&dc->ce_pull, &dc->ce_fold, &dc->ce_push})
+        if (*s) { cudaStreamSynchronize(*s); cudaStreamDestroy(*s); *s = nullptr; }
+    for (int i = 0; i < 4; ++i) {
+        if (dc->ce_pulled[i]) cudaEventDestroy(dc->ce_pulled[i]);
+        if (dc->ce_folded[i]) cudaEventDestroy(dc->ce_folded[i]);
+        dc->ce_pulled[i] = dc->ce_folded[i] = nullptr;
+    }
+    if (dc->ce_start) cudaEventDestroy(dc->ce_start);
+    if (dc->ce_end) cudaEventDestroy(dc->ce_end);
+    dc->ce_start = dc->ce_end = nullptr;
+    if (dc->ce_scratch) cudaFree(dc->ce_scratch);
+    dc->ce_scratch = nullptr;
+    dc->ce_scratch_bytes = 0;
+}
+
 void destroy_context(cail_dev_comm *dc) {
     if (!dc) return;
     if (dc->ok) {
@@ -575,6 +606,7 @@ void destroy_context(cail_dev_comm *dc) {
         if (dc->dev >= 0) cudaSetDevice(dc->dev);
         if (dc->stream) cudaStreamSynchronize(dc->stream);
         nvls_teardown(dc);
+        ce_teardown(dc);
         for (auto &kv : dc->imports) cudaIpcCloseMemHandle(kv.second.base);
         dc->imports.clear();
         for (int q = 0; q < dc->P; ++q)
@@ -614,7 +646,7 @@ cail_dev_comm *create_context(MPI_Comm comm) {
     CUdevice cd;
     if (g_drv.deviceGet && g_drv.deviceGetAttribute && g_drv.deviceGet(&cd, dc->dev) == CUDA_SUCCESS)
         g_drv.deviceGetAttribute(&mc, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, cd);
-    me.nvls_capable = mc;
+    me.nvls_capable = mc && nvls_wanted(dc->P);  // every rank must want it, or none sets it up
     std::vector<ProbeInfo> all(dc->P);
     if (PMPI_Allgather(&me, sizeof(me), MPI_BYTE, all.data(), sizeof(me), MPI_BYTE, comm) != MPI_SUCCESS)
         ok = false;
@@ -777,7 +809,130 @@ int run_oneshot_chunked(cail_dev_comm *dc, const char *src, char *dst, size_t co
 }
 
 // ---- two-shot over registered user buffers
-int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec) {
+// ---- copy-engine two-shot
+// Rank r owns slice r of the message (cut at 16-byte units).  For each chunk
+// of its slice the copy engine pulls the P-1 peers' parts into local scratch
+// (stream ce_pull), a fold kernel reduces them with the local part in rank
+// order into this rank's output (ce_fold), and the copy engine pushes the
+// result into every peer's output (ce_push); the three stages of successive
+// chunks overlap.  Chunks rotate through CAIL_CE_BUFFERS (2..4, default 4)
+// scratch buffers, and the pulls into a buffer wait for the fold that last
+// read it.  Only copy
+// engines touch NVLink: with both directions busy they move 773 GB/s per
+// direction on B200, against 704 for SM stores and 664 for SM loads.
+constexpr size_t kCeScratchMax = (size_t)512 << 20;
+
+int ce_buffers() {
+    static const int v = [] {
+        const char *e = getenv("CAIL_CE_BUFFERS");
+        int b = e ? atoi(e) : 4;
+        return b >= 2 && b <= 4 ? b : 4;
+    }();
+    return v;
+}
+
+bool ce_ensure(cail_dev_comm *dc, size_t scratch) {
+    bool ok = true;
+    for (cudaStream_t *s : {&dc->ce_pull, &dc->ce_fold, &dc->ce_push})
+        if (!*s) ok = ok && cudaStreamCreateWithFlags(s, cudaStreamNonBlocking) == cudaSuccess;
+    for (int i = 0; i < 4; ++i) {
+        if (!dc->ce_pulled[i]) ok = ok && cudaEventCreateWithFlags(&dc->ce_pulled[i], cudaEventDisableTiming) == cudaSuccess;
+        if (!dc->ce_folded[i]) ok = ok && cudaEventCreateWithFlags(&dc->ce_folded[i], cudaEventDisableTiming) == cudaSuccess;
+    }
+    if (!dc->ce_start) ok = ok && cudaEventCreateWithFlags(&dc->ce_start, cudaEventDisableTiming) == cudaSuccess;
+    if (!dc->ce_end) ok = ok && cudaEventCreateWithFlags(&dc->ce_end, cudaEventDisableTiming) == cudaSuccess;
+    if (ok && dc->ce_scratch_bytes < scratch) {
+        if (dc->ce_scratch) cudaFree(dc->ce_scratch);
+        dc->ce_scratch = nullptr;
+        dc->ce_scratch_bytes = 0;
+        ok = cudaMalloc(&dc->ce_scratch, scratch) == cudaSuccess;
+        if (ok) dc->ce_scratch_bytes = scratch;
+    }
+    return ok;
+}
+
+size_t ce_chunk_bytes(size_t slice_bytes, int P) {
+    // CAIL_CE_CHUNK (bytes) overrides: a sixteenth of the slice, 2..32 MiB,
+    // and at most the scratch bound over all buffers
+    static const size_t env = [] {
+        const char *e = getenv("CAIL_CE_CHUNK");
+        return e ? (size_t)atoll(e) : (size_t)0;
+    }();
+    size_t c = env ? env : slice_bytes / 16;
+    if (!env) c = c < ((size_t)2 << 20) ? ((size_t)2 << 20) : (c > ((size_t)32 << 20) ? ((size_t)32 << 20) : c);
+    const size_t nb = (size_t)ce_buffers();
+    if (P > 1 && c > kCeScratchMax / (nb * (size_t)(P - 1))) c = kCeScratchMax / (nb * (size_t)(P - 1));
+    c = (c + (1 << 16) - 1) >> 16 << 16;  // 64 KiB units
+    return c ? c : (size_t)1 << 16;
+}
+
+int ce_body(cail_dev_comm *dc, const char *const *srcs, char *const *dsts, size_t count, size_t esz, int op,
+            int ec) {
+    const int P = dc->P, r = dc->rank;
+    const size_t unit = 16 / esz;
+    const size_t nunits = count / unit;
+    const size_t lo = nunits * r / P * unit;
+    const size_t hi = r == P - 1 ? count : nunits * (r + 1) / P * unit;
+    const size_t chunk = ce_chunk_bytes((hi - lo) * esz, P);
+    const size_t celems = chunk / esz;
+    const int nb = ce_buffers();
+    const size_t scratch = P > 1 ? (size_t)nb * (size_t)(P - 1) * chunk : 16;
+    if (!ce_ensure(dc, scratch)) {
+        CAIL_ERR("ce_two_shot: cannot create streams, events or %zu bytes of scratch", scratch);
+        dc->broken = true;
+        return MPI_ERR_OTHER;
+    }
+    double tl = cail_global_state.profile ? cail_now_us() : 0.0;
+    bool ok = cudaEventRecord(dc->ce_start, dc->stream) == cudaSuccess;
+    for (cudaStream_t s : {dc->ce_pull, dc->ce_fold, dc->ce_push})
+        ok = ok && cudaStreamWaitEvent(s, dc->ce_start, 0) == cudaSuccess;
+    size_t c = 0;
+    for (size_t off = lo; ok && off < hi; off += celems, ++c) {
+        const size_t n = hi - off < celems ? hi - off : celems;
+        const int buf = (int)(c % (size_t)nb);
+        char *base = P > 1 ? dc->ce_scratch + (size_t)buf * (size_t)(P - 1) * chunk : dc->ce_scratch;
+        if (c >= (size_t)nb) ok = ok && cudaStreamWaitEvent(dc->ce_pull, dc->ce_folded[buf], 0) == cudaSuccess;
+        cail::FoldArgs f;
+        memset(&f, 0, sizeof(f));
+        f.P = P;
+        f.count = n;
+        f.dst = dsts[r] + off * esz;
+        for (int q = 0, s = 0; q < P; ++q) {
+            if (q == r) {
+                f.src[q] = srcs[r] + off * esz;
+                continue;
+            }
+            char *slot = base + (size_t)s++ * chunk;
+            f.src[q] = slot;
+            ok = ok && cudaMemcpyAsync(slot, srcs[q] + off * esz, n * esz, cudaMemcpyDefault, dc->ce_pull) == cudaSuccess;
+        }
+        ok = ok && cudaEventRecord(dc->ce_pulled[buf], dc->ce_pull) == cudaSuccess;
+        ok = ok && cudaStreamWaitEvent(dc->ce_fold, dc->ce_pulled[buf], 0) == cudaSuccess;
+        const size_t want = (n * esz / 16 + 1023) / 1024;
+        const int blocks = (int)(want < 1 ? 1 : (want > (size_t)dc->sms * 2 ? (size_t)dc->sms * 2 : want));
+        ok = ok && cail::launch_fold(op, ec, f, blocks, 512, dc->ce_fold) == cudaSuccess;
+        cail_counters.launches++;
+        ok = ok && cudaEventRecord(dc->ce_folded[buf], dc->ce_fold) == cudaSuccess;
+        ok = ok && cudaStreamWaitEvent(dc->ce_push, dc->ce_folded[buf], 0) == cudaSuccess;
+        for (int q = 0; q < P; ++q)
+            if (q != r)
+                ok = ok && cudaMemcpyAsync(dsts[q] + off * esz, dsts[r] + off * esz, n * esz, cudaMemcpyDefault,
+                                           dc->ce_push) == cudaSuccess;
+    }
+    ok = ok && cudaEventRecord(dc->ce_end, dc->ce_push) == cudaSuccess;
+    ok = ok && cudaStreamWaitEvent(dc->stream, dc->ce_end, 0) == cudaSuccess;
+    cail_prof_mark(CAIL_PH_LAUNCH, tl);
+    if (!ok) {
+        CAIL_ERR("ce_two_shot: enqueue failed: %s", cudaGetErrorString(cudaGetLastError()));
+        cudaStreamSynchronize(dc->ce_push);
+        dc->broken = true;
+        return MPI_ERR_OTHER;
+    }
+    return check_status(dc, "ce_two_shot");
+}
+
+int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec,
+                bool ce = false) {
     XSlot &me = dc->xs[dc->rank];
     // Peers read this rank's buffers as soon as it arrives, so its pending
     // legacy-stream writes must have landed first.
@@ -820,6 +975,11 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
             dc->broken = true;
             return MPI_ERR_OTHER;
         }
+        if (ce) {
+            rc = ce_body(dc, a.src, a.dst, count, esz, op, ec);
+            goto depart;
+        }
+        {
         uint64_t mis = (uint64_t)(uintptr_t)src & 15;
         bool vec_ok = true;
         for (int q = 0; q < dc->P; ++q)
@@ -862,7 +1022,9 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
         } else {
             rc = check_status(dc, "two_shot");
         }
+        }
     }
+depart:
     // depart: peers may only return (and reuse their buffers) once every
     // rank's kernel has finished reading and writing them
     me.depart.store(seq, std::memory_order_release);
@@ -936,9 +1098,12 @@ size_t default_oneshot_max(int P) {
 
 // NVLS moves about N(1 + 1/P) bytes per GPU and direction plus a local
 // copy-in and copy-out, against 2N(P-1)/P for two-shot: it can only win at
-// large P.  Measured on 2 x B200 it reaches 44% of two-shot, so auto mode
-// uses it from CAIL_NVLS_MIN_RANKS ranks (default 8) and CAIL_NVLS_MIN
-// bytes (default 16 MiB).
+// large P.  Measured on B200 (1 GiB, float sum) it stays below two-shot at
+// every rank count: 311 vs 670 GB/s bus bandwidth at 2 ranks, 503 vs 670 at
+// 4, 594 vs 616-646 at 8.  multimem.ld_reduce + multimem.st alone move 544
+// GB/s per direction at 8 ranks, and the staging copies cost the rest.  So
+// auto mode uses NVLS only when CAIL_NVLS_MIN_RANKS (default 0: never) is
+// set and reached, from CAIL_NVLS_MIN bytes (default 16 MiB).
 size_t nvls_min_bytes() {
     static const size_t v = [] {
         const char *e = getenv("CAIL_NVLS_MIN");
@@ -947,10 +1112,20 @@ size_t nvls_min_bytes() {
     return v;
 }
 
+// Auto mode hands messages of at least CAIL_CE_MIN bytes to the
+// copy-engine two-shot.
+size_t ce_min_bytes() {
+    static const size_t v = [] {
+        const char *e = getenv("CAIL_CE_MIN");
+        return e ? (size_t)atoll(e) : ~(size_t)0;
+    }();
+    return v;
+}
+
 int nvls_min_ranks() {
     static const int v = [] {
         const char *e = getenv("CAIL_NVLS_MIN_RANKS");
-        return e ? atoi(e) : 8;
+        return e ? atoi(e) : 0;
     }();
     return v;
 }
@@ -988,8 +1163,9 @@ int cail_dev_pick_algo(cail_dev_comm *dc, size_t bytes, int count, cail_datatype
                                    : (s.msg_small_threshold_set ? s.msg_small_threshold - 1
                                                                 : default_oneshot_max(dc->P));
     if (bytes <= one_max) return CAIL_ALGO_ONE_SHOT;
-    if (dc->P >= nvls_min_ranks() && cail_dev_nvls_ok(dc, dt, op) && bytes >= nvls_min_bytes())
+    if (nvls_min_ranks() > 0 && dc->P >= nvls_min_ranks() && cail_dev_nvls_ok(dc, dt, op) && bytes >= nvls_min_bytes())
         return CAIL_ALGO_NVLS;
+    if (bytes >= ce_min_bytes()) return CAIL_ALGO_CE_TWO_SHOT;
     return CAIL_ALGO_TWO_SHOT;
 }
 
@@ -1032,6 +1208,8 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
         rc = run_oneshot_chunked(dc, src, dst, (size_t)count, esz, (int)op, ec);
     } else if (algo == CAIL_ALGO_NVLS && cail_dev_nvls_ok(dc, dt, op)) {
         rc = run_nvls(dc, src, dst, (size_t)count, esz, (int)op, ec);
+    } else if (algo == CAIL_ALGO_CE_TWO_SHOT) {
+        rc = run_twoshot(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
     } else {
         rc = run_twoshot(dc, src, dst, (size_t)count, esz, (int)op, ec);
     }

@@ -429,6 +429,53 @@ __global__ void __launch_bounds__(512, 2) nvls_kernel(NvlsArgs a) {
     }
 }
 
+// ---------------------------------------------------------------- fold
+// dst = src[0] op src[1] op ... op src[P-1], all local memory; 16-byte
+// vectors when every pointer is 16-byte aligned, two per iteration.
+template <int OP, typename T>
+__global__ void __launch_bounds__(512) fold_kernel(FoldArgs a) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    uintptr_t mis = (uintptr_t)a.dst;
+    for (int q = 0; q < a.P; ++q) mis |= (uintptr_t)a.src[q];
+    const size_t nv = (mis & 15) == 0 ? a.count * sizeof(T) / 16 : 0;
+    size_t i = tid;
+    for (; i + stride < nv; i += 2 * stride) {
+        uint4 v0[kMaxRanks], v1[kMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+            if (q < a.P) {
+                v0[q] = ld_v4(a.src[q] + i * 16);
+                v1[q] = ld_v4(a.src[q] + (i + stride) * 16);
+            }
+        uint4 acc0 = v0[0], acc1 = v1[0];
+#pragma unroll
+        for (int q = 1; q < kMaxRanks; ++q)
+            if (q < a.P) {
+                acc0 = vop<OP, T>(acc0, v0[q]);
+                acc1 = vop<OP, T>(acc1, v1[q]);
+            }
+        st_v4(a.dst + i * 16, acc0);
+        st_v4(a.dst + (i + stride) * 16, acc1);
+    }
+    for (; i < nv; i += stride) {
+        uint4 v[kMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+            if (q < a.P) v[q] = ld_v4(a.src[q] + i * 16);
+        uint4 acc = v[0];
+#pragma unroll
+        for (int q = 1; q < kMaxRanks; ++q)
+            if (q < a.P) acc = vop<OP, T>(acc, v[q]);
+        st_v4(a.dst + i * 16, acc);
+    }
+    for (size_t e = nv * 16 / sizeof(T) + tid; e < a.count; e += stride) {
+        T acc = reinterpret_cast<const T *>(a.src[0])[e];
+        for (int q = 1; q < a.P; ++q) acc = apply<OP, T>(acc, reinterpret_cast<const T *>(a.src[q])[e]);
+        reinterpret_cast<T *>(a.dst)[e] = acc;
+    }
+}
+
 // ---------------------------------------------------------------- local reduce
 template <int OP, typename T>
 __global__ void __launch_bounds__(256) reduce_local_kernel(const T *__restrict__ in,
@@ -472,6 +519,15 @@ struct LaunchTwoShot {
             twoshot_kernel<OP, typename EcType<EC>::T, true><<<b, t, 0, s>>>(a);
         else
             twoshot_kernel<OP, typename EcType<EC>::T, false><<<b, t, 0, s>>>(a);
+    }
+};
+
+struct LaunchFold {
+    const FoldArgs &a;
+    int b, t;
+    cudaStream_t s;
+    template <int OP, int EC> void operator()() {
+        fold_kernel<OP, typename EcType<EC>::T><<<b, t, 0, s>>>(a);
     }
 };
 
@@ -529,6 +585,12 @@ cudaError_t launch_oneshot(int op, int ec, const OneShotArgs &a, int blocks, int
 cudaError_t launch_twoshot(int op, int ec, const TwoShotArgs &a, int blocks, int threads,
                            cudaStream_t s) {
     LaunchTwoShot l{a, blocks, threads, s};
+    if (!dispatch_op_class(op, ec, l)) return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fold(int op, int ec, const FoldArgs &a, int blocks, int threads, cudaStream_t s) {
+    LaunchFold l{a, blocks, threads, s};
     if (!dispatch_op_class(op, ec, l)) return cudaErrorInvalidValue;
     return cudaGetLastError();
 }

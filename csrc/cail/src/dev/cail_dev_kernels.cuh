@@ -87,6 +87,16 @@ struct NvlsArgs {
     DevStatus *status;
 };
 
+// Rank-order fold of P local sources into dst: dst = src[0] op src[1] op ...
+// (the copy-engine two-shot reduces its slice of each chunk with it, after
+// the copy engines have pulled the peers' parts into local scratch).
+struct FoldArgs {
+    const char *src[kMaxRanks];
+    char *dst;
+    size_t count;                    // elements
+    int P;
+};
+
 // Launchers: return cudaSuccess or the launch error.  ec is a
 // cail_elem_class_t, op a cail_op_t.
 cudaError_t launch_oneshot(int op, int ec, const OneShotArgs &a, int blocks, int threads,
@@ -94,6 +104,7 @@ cudaError_t launch_oneshot(int op, int ec, const OneShotArgs &a, int blocks, int
 cudaError_t launch_twoshot(int op, int ec, const TwoShotArgs &a, int blocks, int threads,
                            cudaStream_t s);
 cudaError_t launch_nvls(int op, int ec, const NvlsArgs &a, int blocks, int threads, cudaStream_t s);
+cudaError_t launch_fold(int op, int ec, const FoldArgs &a, int blocks, int threads, cudaStream_t s);
 // 1 if the NVLS kernel exists for (op, ec).
 int nvls_supported(int op, int ec);
 // Element-wise local reduction io = op(io, in) (PMPI algorithm path).

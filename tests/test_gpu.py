@@ -45,7 +45,7 @@ def test_native_library_loaded_in_process():
     assert os.path.join(LIB, "libcail.so") in r.stdout
 
 
-@pytest.mark.parametrize("algo", ["one_shot", "two_shot"])
+@pytest.mark.parametrize("algo", ["one_shot", "two_shot", "ce_two_shot"])
 def test_single_rank_kernels_all_types(algo):
     need_gpus(1)
     r = mpirun(1, ["cail_check", "-m", "matrix", "-c", "100003", "-d", "-p", "--bits"], preload="cuda",
@@ -99,7 +99,7 @@ def nranks():
 
 
 @pytest.mark.multigpu
-@pytest.mark.parametrize("algo", ["one_shot", "two_shot"])
+@pytest.mark.parametrize("algo", ["one_shot", "two_shot", "ce_two_shot"])
 def test_nvlink_p2p_matrix_bit_exact(algo):
     # counts {1,2,3,4099,4100,4102}: heads, tails, fewer elements than ranks;
     # separate and in place; floats bit-identical to the rank-order oracle
@@ -111,14 +111,14 @@ def test_nvlink_p2p_matrix_bit_exact(algo):
 
 
 @pytest.mark.multigpu
-@pytest.mark.parametrize("algo", ["auto", "nvls", "two_shot"])
+@pytest.mark.parametrize("algo", ["auto", "nvls", "two_shot", "ce_two_shot"])
 def test_nvlink_config3_coverage(algo):
     """20 datatypes x SUM/PROD/MAX/MIN at counts 1,000,003 and 4,194,304 at
     every available rank count; integers bit-exact, floats within
-    reassociation tolerance (NVLS) or bit-exact (two-shot)."""
+    reassociation tolerance (NVLS) or bit-exact (two-shot, both kinds)."""
     need_gpus(2)
     for np in nranks():
-        args = ["cail_check", "-m", "config3", "-d"] + (["--bits"] if algo == "two_shot" else ["--tol", "1e-4"])
+        args = ["cail_check", "-m", "config3", "-d"] + (["--bits"] if algo in ("two_shot", "ce_two_shot") else ["--tol", "1e-4"])
         r = mpirun(np, args, preload="cuda", env={"CAIL_ALGO": algo}, timeout=1200)
         assert ok(r), f"np={np} algo={algo}\n" + r.stdout[-3000:] + r.stderr[-3000:]
 
