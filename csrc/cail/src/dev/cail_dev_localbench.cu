@@ -4,7 +4,9 @@
 // P-rank communicator with every "peer" emulated by a separate buffer on
 // the current GPU: the two-shot kernel reads P inputs and writes P outputs,
 // the one-shot kernel pushes into P scratch areas and folds P slots, with
-// its peers' arrival flags set in advance (so it never waits).  The
+// its peers' arrival flags set in advance (so it never waits).  The fold
+// kernel of the copy-engine two-shot runs on P local sources as it does in
+// production (there it is local already).  The
 // instruction stream is the production one; only NVLink is replaced by
 // local HBM.  This is the case a profiler can capture on one GPU.
 #include <cuda_runtime.h>
@@ -33,7 +35,7 @@ struct Bufs {
 
 }  // namespace
 
-// kernel: 0 = one_shot, 1 = two_shot.  Runs `iters` launches of a float SUM
+// kernel: 0 = one_shot, 1 = two_shot, 2 = fold (P sources of `bytes`).  Runs `iters` launches of a float SUM
 // over `bytes` bytes per rank with P emulated ranks (2..8) and writes the
 // mean time per launch in milliseconds to *ms.  Returns 0 or -1.
 extern "C" int cail_bench_kernel_local(int kernel, int P, size_t bytes, int iters, float *ms) {
@@ -83,6 +85,23 @@ extern "C" int cail_bench_kernel_local(int kernel, int P, size_t bytes, int iter
         cail::launch_oneshot(CAIL_SUM, CAIL_EC_F32, a, blocks, 512, s);  // warm-up
         cudaEventRecord(e0, s);
         for (int i = 0; i < iters; ++i) cail::launch_oneshot(CAIL_SUM, CAIL_EC_F32, a, blocks, 512, s);
+        cudaEventRecord(e1, s);
+    } else if (kernel == 2) {
+        cail::FoldArgs a;
+        memset(&a, 0, sizeof(a));
+        for (int q = 0; q < P; ++q) {
+            a.src[q] = b.get(bytes);
+            if (!a.src[q]) { rc = -1; goto out; }
+        }
+        a.dst = b.get(bytes);
+        if (!a.dst) { rc = -1; goto out; }
+        a.P = P;
+        a.count = count;
+        size_t want = (bytes / 16 + 1023) / 1024;
+        int blocks = (int)(want > (size_t)(sms * 2) ? sms * 2 : (want < 1 ? 1 : want));
+        cail::launch_fold(CAIL_SUM, CAIL_EC_F32, a, blocks, 512, s);
+        cudaEventRecord(e0, s);
+        for (int i = 0; i < iters; ++i) cail::launch_fold(CAIL_SUM, CAIL_EC_F32, a, blocks, 512, s);
         cudaEventRecord(e1, s);
     } else {
         cail::TwoShotArgs a;
