@@ -132,6 +132,15 @@ def test_ring_count_below_nprocs_warns():
     assert "ring: count=3 < nprocs=4, cannot distribute chunks, falling back to PMPI" in r.stderr
 
 
+@pytest.mark.parametrize("algo", ["one_shot", "two_shot", "nvls", "ce_two_shot"])
+def test_forced_device_algorithm_on_host_build_warns(algo):
+    # the NVLink algorithms exist only in the CUDA build: the host-only build
+    # names the forced algorithm, warns and forwards to PMPI_Allreduce
+    r = mpirun(2, ["cail_check", "-m", "basic"], env={"CAIL_ALGO": algo, "CAIL_MIN_MSG_SIZE": "0"})
+    assert ok(r), r.stdout + r.stderr
+    assert f"[cail WARN] forced {algo} needs the CUDA build, falling back to PMPI" in r.stderr
+
+
 # ---------------------------------------------------------------- logging / env
 def test_unsupported_type_warns_and_warn_zero_silences():
     r = mpirun(2, ["cail_check", "-m", "edge"])
