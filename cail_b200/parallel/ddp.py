@@ -89,6 +89,11 @@ class BucketedAllreduce:
 
     def _worker(self) -> None:
         dt, op = _lib.H["MPI_FLOAT"], _lib.H["MPI_SUM"]
+        # A new thread starts on device 0.  CUDA-aware MPIs (the reference
+        # among them) allocate scratch and launch on the calling thread's
+        # current device, so it must be the buckets' device.
+        if self.flats and self.flats[0].is_cuda:
+            torch.cuda.set_device(self.flats[0].device)
         while True:
             item = self.q.get()
             if item is None:

@@ -74,7 +74,8 @@ __device__ __forceinline__ unsigned long long gtime() {
 
 // ---------------------------------------------------------------- kernels
 // P2P: npeer chunks of n16 16-byte vectors each; push stores local data into
-// the peers, pull loads the peers' data into local memory.
+// the peers, pull loads the peers' data into local memory.  Consecutive
+// vectors go to consecutive peers, so every link carries traffic at once.
 template <bool PUSH>
 __global__ void __launch_bounds__(512) p2p_kernel(const uint4 *const *peer_src, uint4 *const *peer_dst,
                                                   const uint4 *local_src, uint4 *local_dst, int npeer, size_t n16) {
@@ -87,13 +88,13 @@ __global__ void __launch_bounds__(512) p2p_kernel(const uint4 *const *peer_src, 
 #pragma unroll
         for (int q = 0; q < U; ++q) {
             const size_t w = i + q * nt;
-            if (w < total) v[q] = PUSH ? local_src[w] : peer_src[w / n16][w % n16];
+            if (w < total) v[q] = PUSH ? local_src[w] : peer_src[w % npeer][w / npeer];
         }
 #pragma unroll
         for (int q = 0; q < U; ++q) {
             const size_t w = i + q * nt;
             if (w < total) {
-                if (PUSH) peer_dst[w / n16][w % n16] = v[q];
+                if (PUSH) peer_dst[w % npeer][w / npeer] = v[q];
                 else local_dst[w] = v[q];
             }
         }
@@ -242,12 +243,12 @@ static void probe_p2p(int n, int sms) {
     for (int d = 0; d < n; ++d) {
         std::vector<const uint4 *> hs;
         std::vector<uint4 *> hd;
-        for (int e = 0; e < n; ++e)
-            if (e != d) {
-                const int slot = d < e ? d : d - 1;  // d's chunk inside peer e's buffer
-                hs.push_back((const uint4 *)(a[e] + (size_t)slot * per));
-                hd.push_back((uint4 *)(b[e] + (size_t)slot * per));
-            }
+        for (int k = 1; k < n; ++k) {  // peers in the order d+1, d+2, ...: no common first target
+            const int e = (d + k) % n;
+            const int slot = d < e ? d : d - 1;  // d's chunk inside peer e's buffer
+            hs.push_back((const uint4 *)(a[e] + (size_t)slot * per));
+            hd.push_back((uint4 *)(b[e] + (size_t)slot * per));
+        }
         CR(cudaSetDevice(d));
         CR(cudaMalloc(&ps[d], sizeof(void *) * hs.size()));
         CR(cudaMalloc(&pd[d], sizeof(void *) * hd.size()));
@@ -267,12 +268,11 @@ static void probe_p2p(int n, int sms) {
                moved / tpush / 1e9);
     }
     double tce = time_all(n, st, 5, [&](int d, cudaStream_t s) {
-        for (int e = 0, k = 0; e < n; ++e)
-            if (e != d) {
-                const int slot = d < e ? d : d - 1;
-                CR(cudaMemcpyPeerAsync(b[e] + (size_t)slot * per, e, a[d] + (size_t)k * per, d, per, s));
-                ++k;
-            }
+        for (int k = 1; k < n; ++k) {
+            const int e = (d + k) % n;
+            const int slot = d < e ? d : d - 1;
+            CR(cudaMemcpyPeerAsync(b[e] + (size_t)slot * per, e, a[d] + (size_t)(k - 1) * per, d, per, s));
+        }
     });
     printf("p2p copy_engine_push %.1f GB/s\n", moved / tce / 1e9);
     for (int d = 0; d < n; ++d) {

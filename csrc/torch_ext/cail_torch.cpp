@@ -4,7 +4,10 @@
 // (cail-b200's, or the reference's for comparison runs), so the extension
 // never resolves MPI symbols itself and cannot bind to the wrong library.
 // The call releases the GIL: the data-parallel harness issues it from a
-// communication thread while the main thread keeps launching backward.
+// communication thread while the main thread keeps launching backward.  The
+// tensor's device is made current for the call (a CUDA-aware MPI allocates
+// and launches on the caller's current device).
+#include <c10/core/DeviceGuard.h>
 #include <torch/extension.h>
 
 #include <cstdint>
@@ -26,6 +29,7 @@ int64_t allreduce_inplace(const at::Tensor &t, int64_t datatype, int64_t op, int
     TORCH_CHECK(t.numel() < (int64_t(1) << 31), "cail_torch: MPI counts are int");
     void *p = t.data_ptr();
     int n = static_cast<int>(t.numel());
+    c10::DeviceGuard guard(t.device());
     int rc;
     {
         pybind11::gil_scoped_release nogil;
@@ -43,6 +47,7 @@ int64_t allreduce(const at::Tensor &src, const at::Tensor &dst, int64_t datatype
     const void *s = src.data_ptr();
     void *d = dst.data_ptr();
     int n = static_cast<int>(src.numel());
+    c10::DeviceGuard guard(dst.device());
     int rc;
     {
         pybind11::gil_scoped_release nogil;
