@@ -297,10 +297,10 @@ def main() -> None:
         del h_in, h_out
 
     # ---------------- sweep
-    sweep = []
-    if not args.no_sweep:
-        nbytes = args.sweep_min
-        while nbytes <= min(args.sweep_max, args.bytes):
+    def run_sweep(lo: int, hi: int) -> list:
+        rows = []
+        nbytes = lo
+        while nbytes <= hi:
             n = nbytes // 4
             s, r = send[:n], recv[:n]
             iters = args.sweep_iters if nbytes <= (128 << 20) else max(10, args.sweep_iters // 5)
@@ -323,8 +323,21 @@ def main() -> None:
             if args.impl == "ours":
                 import cail_b200
                 row["algo"] = cail_b200.last_algorithm()
-            sweep.append(row)
+            rows.append(row)
             nbytes *= 2
+        return rows
+
+    sweep, sweep_ordered = [], []
+    if not args.no_sweep:
+        sweep = run_sweep(args.sweep_min, min(args.sweep_max, args.bytes))
+        if args.impl == "ours" and P > 1:
+            # small messages again with stream-ordered completion (the call
+            # returns once queued, like NCCL's): the same events then time the
+            # device work instead of the host round trip of a blocking call
+            import cail_b200
+            prev = cail_b200.set_stream_ordered(True)
+            sweep_ordered = run_sweep(args.sweep_min, min(512 << 10, args.sweep_max, args.bytes))
+            cail_b200.set_stream_ordered(bool(prev))
     clocks.__exit__(None, None, None)
     clock_summary = clocks.summary()
     if clock_summary is not None:
@@ -360,6 +373,7 @@ def main() -> None:
         "gpu_launches": (l1 - l0) if (l0 is not None and l1 is not None) else None,
         "algorithm": algo,
         "sweep": sweep,
+        "sweep_stream_ordered": sweep_ordered,
     }
     if rank == 0:
         print(json.dumps(out), flush=True)

@@ -72,6 +72,17 @@ def last_algorithm() -> Optional[str]:
     return libs.cail.cail_last_algorithm().decode()
 
 
+def set_stream_ordered(on: bool) -> Optional[bool]:
+    """Stream-ordered completion of small (one-shot) allreduces: the call
+    returns once the kernel is queued and the legacy default stream waits for
+    it, as with NCCL; the default (False) is MPI's host-synchronous return.
+    Returns the previous mode (None when the loaded interposer is not ours)."""
+    libs = _lib.loaded()
+    if libs is None or libs.impl != "ours":
+        return None
+    return bool(libs.cail.cail_set_stream_ordered(1 if on else 0))
+
+
 class Stats(ctypes.Structure):
     _fields_ = [("calls", ctypes.c_ulonglong), ("passthrough", ctypes.c_ulonglong),
                 ("by_algo", ctypes.c_ulonglong * 8), ("bytes", ctypes.c_ulonglong),

@@ -125,6 +125,8 @@ def load(impl: str = "ours", host: bool = False) -> Libs:
         cail.cail_version.restype = ctypes.c_char_p
         cail.cail_comm_uses_nvlink.argtypes = [ctypes.c_int]
         cail.cail_comm_uses_nvls.argtypes = [ctypes.c_int]
+        cail.cail_set_stream_ordered.argtypes = [ctypes.c_int]
+        cail.cail_set_stream_sync.argtypes = [ctypes.c_int]
     _loaded = Libs(mpi=mpi, cail=cail, impl=impl, path=path)
     return _loaded
 

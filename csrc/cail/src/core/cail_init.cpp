@@ -29,7 +29,7 @@ cail_state_t cail_global_state = {
     /*force_algo*/ CAIL_ALGO_AUTO,
     /*device_timeout_ms*/ CAIL_DEFAULT_DEVICE_TIMEOUT_MS,
     /*nvls*/ 1, /*oneshot_max*/ 0, /*flush_recv*/ 1, /*stats*/ 0, /*trace*/ nullptr,
-    /*stream_sync*/ 1, /*profile*/ 0};
+    /*stream_sync*/ 1, /*profile*/ 0, /*stream_ordered*/ 0};
 
 cail_stats_t cail_counters;
 int cail_last_algo = -2;  // -2: none yet, -3: passthrough
@@ -58,6 +58,7 @@ const char *env_nonempty(const char *name) {
 }
 
 bool g_stream_sync_set = false;  // cail_set_stream_sync() overrides the environment
+bool g_stream_ordered_set = false;  // likewise cail_set_stream_ordered()
 
 }  // namespace
 
@@ -151,6 +152,7 @@ int cail_init(MPI_Comm comm) {
     if ((e = env_nonempty(CAIL_ENV_STATS))) s.stats = e[0] != '0';
     if ((e = env_nonempty("CAIL_PROFILE"))) s.profile = e[0] != '0';
     if ((e = env_nonempty(CAIL_ENV_STREAM_SYNC)) && !g_stream_sync_set) s.stream_sync = e[0] != '0';
+    if ((e = env_nonempty(CAIL_ENV_STREAM_ORDERED)) && !g_stream_ordered_set) s.stream_ordered = e[0] != '0';
     if ((e = env_nonempty(CAIL_ENV_TRACE))) {
         s.trace = fopen(e, "a");
         if (!s.trace) CAIL_ERR("cannot open CAIL_TRACE file '%s'", e);
@@ -224,6 +226,13 @@ int cail_set_stream_sync(int mode) {
     int prev = cail_global_state.stream_sync;
     cail_global_state.stream_sync = mode ? 1 : 0;
     g_stream_sync_set = true;
+    return prev;
+}
+
+int cail_set_stream_ordered(int mode) {
+    int prev = cail_global_state.stream_ordered;
+    cail_global_state.stream_ordered = mode ? 1 : 0;
+    g_stream_ordered_set = true;
     return prev;
 }
 

@@ -37,6 +37,7 @@
 #define CAIL_ENV_TRACE "CAIL_TRACE"
 #define CAIL_ENV_FLUSH_RECV "CAIL_FLUSH_RECV"
 #define CAIL_ENV_STREAM_SYNC "CAIL_STREAM_SYNC"
+#define CAIL_ENV_STREAM_ORDERED "CAIL_STREAM_ORDERED"
 
 #define CAIL_DEFAULT_MSG_SMALL_THRESHOLD 262144U /* 256 KiB */
 #define CAIL_DEFAULT_NPROCS_THRESHOLD 4U
@@ -68,6 +69,7 @@ typedef struct cail_state {
     FILE *trace;
     int stream_sync;             /* order device work after the legacy stream */
     int profile;                 /* CAIL_PROFILE: host-side phase timers */
+    int stream_ordered;          /* one-shot calls complete in stream order, not on the host */
 } cail_state_t;
 
 /* Opt-in host-side phase timers (CAIL_PROFILE=1), averaged per call and

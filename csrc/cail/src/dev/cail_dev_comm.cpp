@@ -233,6 +233,8 @@ struct cail_dev_comm {
     int nvls_blocks = 0;
     double last_live_check = 0.0;
     cudaEvent_t legacy_ev = nullptr;  // marks the legacy stream's queue at call entry
+    cudaEvent_t done_ev = nullptr;    // end of a stream-ordered call, waited for by the legacy stream
+    bool pending = false;             // a stream-ordered call has not been checked yet
     // copy-engine two-shot: pull / fold / push streams, per-buffer events and
     // a scratch of kCeMaxBufs x (P-1) chunks (created on first use)
     cudaStream_t ce_pull = nullptr, ce_fold = nullptr, ce_push = nullptr;
@@ -613,8 +615,12 @@ void destroy_context(cail_dev_comm *dc) {
             if (q != dc->rank && dc->peer_ws[q]) cudaIpcCloseMemHandle(dc->peer_ws[q]);
         if (dc->ws) cudaFree(dc->ws);
         if (dc->status_h) cudaFreeHost(dc->status_h);
+        if (dc->pending && dc->status_h && dc->status_h->code != 0)
+            CAIL_ERR("a stream-ordered MPI_Allreduce on this communicator failed: rank %d gave up "
+                     "waiting (block %d, epoch %u)", dc->status_h->rank, dc->status_h->block, dc->status_h->epoch);
         if (dc->stream) cudaStreamDestroy(dc->stream);
         if (dc->legacy_ev) cudaEventDestroy(dc->legacy_ev);
+        if (dc->done_ev) cudaEventDestroy(dc->done_ev);
         if (dc->xs) munmap(dc->xs, dc->xs_bytes);
         if (prev >= 0) cudaSetDevice(prev);
     }
@@ -671,6 +677,7 @@ cail_dev_comm *create_context(MPI_Comm comm) {
     // 2. workspace
     ok = cudaStreamCreateWithFlags(&dc->stream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&dc->legacy_ev, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&dc->done_ev, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaMalloc(&dc->ws, kWorkspaceBytes) == cudaSuccess;
     ok = ok && cudaMemset(dc->ws, 0, kFlagBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
     ok = ok && cudaHostAlloc((void **)&dc->status_h, sizeof(DevStatus), cudaHostAllocMapped) == cudaSuccess;
@@ -797,14 +804,48 @@ int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     return sync ? check_status(dc, "one_shot") : MPI_SUCCESS;
 }
 
+// Stream-ordered completion (cail_set_stream_ordered): the legacy stream
+// waits for the call's kernels and the host returns at once.  This is safe
+// for the one-shot kernel alone: its scratch parity comes back two calls
+// later, and a rank's call k+2 can only start after every peer's call k has
+// finished (stream order on each GPU plus the peers' flags of call k+1).
+bool stream_ordered_ok(const cail_dev_comm *dc) {
+    return cail_global_state.stream_ordered && cail_global_state.stream_sync && dc->done_ev;
+}
+
+int finish_stream_ordered(cail_dev_comm *dc) {
+    if (cudaEventRecord(dc->done_ev, dc->stream) != cudaSuccess ||
+        cudaStreamWaitEvent(cudaStreamLegacy, dc->done_ev, 0) != cudaSuccess) {
+        CAIL_ERR("one_shot: ordering the legacy stream after the call failed");
+        return check_status(dc, "one_shot");
+    }
+    dc->pending = true;
+    return MPI_SUCCESS;
+}
+
+// Reports a device-side timeout of an earlier stream-ordered call (without
+// waiting for the device).
+int poll_pending(cail_dev_comm *dc) {
+    if (!dc->pending || dc->status_h->code == 0) return MPI_SUCCESS;
+    const DevStatus &s = *dc->status_h;
+    CAIL_ERR("an earlier stream-ordered call failed: rank %d gave up after %ld ms waiting for %s %d "
+             "(block %d, epoch %u, saw %u)", s.rank, cail_global_state.device_timeout_ms,
+             s.waited_on >= 0 ? "rank" : "barrier", s.waited_on >= 0 ? s.waited_on : -1 - s.waited_on, s.block,
+             s.epoch, s.seen);
+    memset(dc->status_h, 0, sizeof(DevStatus));
+    dc->broken = true;
+    return MPI_ERR_OTHER;
+}
+
 int run_oneshot_chunked(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz,
-                        int op, int ec) {
+                        int op, int ec, bool allow_ordered = false) {
     size_t per = kSlotBytes / esz;
     for (size_t off = 0; off < count; off += per) {
         size_t n = count - off < per ? count - off : per;
         int rc = run_oneshot(dc, src + off * esz, dst + off * esz, n, esz, op, ec, false);
         if (rc != MPI_SUCCESS) return rc;
     }
+    if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc);
     return check_status(dc, "one_shot");
 }
 
@@ -1177,6 +1218,7 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
         CAIL_ERR("nvlink context of this communicator failed earlier; refusing further calls");
         return MPI_ERR_OTHER;
     }
+    if (poll_pending(dc) != MPI_SUCCESS) return MPI_ERR_OTHER;
     // A rank that left the job is noticed on the host before the next launch
     // (checked at most every 10 ms, so back-to-back calls pay nothing).
     double now = cail_now_us();
@@ -1207,7 +1249,7 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
     cail_prof_mark(CAIL_PH_SETUP, ts);
     // A single rank runs the same kernels (they degenerate to a copy).
     if (algo == CAIL_ALGO_ONE_SHOT) {
-        rc = run_oneshot_chunked(dc, src, dst, (size_t)count, esz, (int)op, ec);
+        rc = run_oneshot_chunked(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
     } else if (algo == CAIL_ALGO_NVLS && cail_dev_nvls_ok(dc, dt, op)) {
         rc = run_nvls(dc, src, dst, (size_t)count, esz, (int)op, ec);
     } else if (algo == CAIL_ALGO_CE_TWO_SHOT) {

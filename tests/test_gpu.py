@@ -144,6 +144,23 @@ def test_registration_cache_stress():
 
 
 @pytest.mark.multigpu
+def test_stream_ordered_small_messages_bit_exact():
+    """CAIL_STREAM_ORDERED=1: one-shot calls return once queued and the legacy
+    stream waits for them; results read back through the legacy stream must
+    be the rank-order oracle's, also over 64 rotating buffers with in-place
+    calls interleaved."""
+    need_gpus(2)
+    env = {"CAIL_ALGO": "one_shot", "CAIL_MIN_MSG_SIZE": "0", "CAIL_STREAM_ORDERED": "1"}
+    for np in nranks():
+        r = mpirun(np, ["cail_check", "-m", "matrix", "-c", "4099", "-d", "-p", "--bits"], preload="cuda",
+                   env=env, timeout=900)
+        assert ok(r), f"np={np}\n" + r.stdout[-3000:] + r.stderr[-3000:]
+        r = mpirun(np, ["cail_check", "-m", "stress", "-c", "32768", "-r", "300", "-b", "64", "-d", "--bits"],
+                   preload="cuda", env=env, timeout=900)
+        assert ok(r), f"np={np}\n" + r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.multigpu
 def test_rank_leaving_between_steps_is_detected():
     need_gpus(2)
     r = mpirun(2, ["cail_check", "-m", "leave", "-d"], preload="cuda",

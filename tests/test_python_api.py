@@ -31,6 +31,15 @@ def test_dtype_mapping():
         mpi_datatype(torch.bfloat16)
 
 
+def test_stream_ordered_toggle_returns_previous_mode():
+    code = ("import ctypes; ctypes.CDLL('build/lib/libmpi.so', mode=ctypes.RTLD_GLOBAL); "
+            "c = ctypes.CDLL('build/lib/libcail.so'); "
+            "print(c.cail_set_stream_ordered(1), c.cail_set_stream_ordered(0), c.cail_set_stream_ordered(0))")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.split() == ["0", "1", "0"]
+
+
 SCRIPT = r"""
 import os, sys, torch
 sys.path.insert(0, %r)
