@@ -71,6 +71,14 @@ int cail_set_stream_sync(int mode);
  * by the next call or at MPI_Finalize.  Returns the previous mode. */
 int cail_set_stream_ordered(int mode);
 
+/* The algorithm auto mode picks for an intercepted device-buffer call of
+ * `bytes` bytes on an NVLink communicator of `nranks` ranks, under this
+ * process' environment (CAIL_ONESHOT_MAX, CAIL_MSG_SMALL_THRESHOLD,
+ * CAIL_NVLS_MIN_RANKS, CAIL_NVLS_MIN, CAIL_CE_MIN, CAIL_NVLS), assuming an
+ * NVSwitch fabric with multicast.  NULL for an unsupported type or op.  Needs
+ * no MPI_Init: for checking a tuning before a job. */
+const char *cail_nvlink_auto_algorithm(int nranks, size_t bytes, MPI_Datatype datatype, MPI_Op op);
+
 #ifdef __cplusplus
 }
 #endif

@@ -96,11 +96,13 @@ void cail_prof_end_call(double total_us) {
     for (int i = 0; i < CAIL_PH_N; ++i) g_call_us[i] = 0.0;
 }
 
-int cail_init(MPI_Comm comm) {
-    (void)comm;
+// Reads the environment into cail_global_state, once per process (the first
+// MPI_Allreduce, or a configuration query before it).
+void cail_load_config(void) {
+    static bool loaded = false;
+    if (loaded) return;
+    loaded = true;
     cail_state_t &s = cail_global_state;
-    if (s.initialized) return MPI_SUCCESS;
-
     const char *e = getenv(CAIL_ENV_DEBUG);
     if (e && e[0] != '\0' && e[0] != '0') s.debug = 1;
     e = getenv(CAIL_ENV_WARN);
@@ -157,6 +159,13 @@ int cail_init(MPI_Comm comm) {
         s.trace = fopen(e, "a");
         if (!s.trace) CAIL_ERR("cannot open CAIL_TRACE file '%s'", e);
     }
+}
+
+int cail_init(MPI_Comm comm) {
+    (void)comm;
+    cail_state_t &s = cail_global_state;
+    if (s.initialized) return MPI_SUCCESS;
+    cail_load_config();
 
     int rc = cail_gpu_init();
     if (rc != 0) {

@@ -100,6 +100,7 @@ double cail_prof_mark(int ph, double t0);
 void cail_prof_end_call(double total_us);
 
 int cail_init(MPI_Comm comm);
+void cail_load_config(void);
 void cail_finalize(void);
 int cail_is_initialized(void);
 

@@ -1173,6 +1173,21 @@ int nvls_min_ranks() {
     return v;
 }
 
+// Auto mode on an NVLink communicator of P ranks; nvls_pair: NVLS is set up
+// and multimem can reduce the call's (type, op).  Depends only on its
+// arguments and the environment.
+int pick_nvlink(int P, size_t bytes, bool nvls_pair) {
+    const cail_state_t &s = cail_global_state;
+    size_t one_max = s.oneshot_max ? s.oneshot_max
+                                   : (s.msg_small_threshold_set ? s.msg_small_threshold - 1
+                                                                : default_oneshot_max(P));
+    if (bytes <= one_max) return CAIL_ALGO_ONE_SHOT;
+    if (nvls_min_ranks() > 0 && P >= nvls_min_ranks() && nvls_pair && bytes >= nvls_min_bytes())
+        return CAIL_ALGO_NVLS;
+    if (bytes >= ce_min_bytes()) return CAIL_ALGO_CE_TWO_SHOT;
+    return CAIL_ALGO_TWO_SHOT;
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- public
@@ -1201,15 +1216,16 @@ int cail_dev_nvls_ok(cail_dev_comm *dc, cail_datatype_t dt, cail_op_t op) {
 
 int cail_dev_pick_algo(cail_dev_comm *dc, size_t bytes, int count, cail_datatype_t dt, cail_op_t op) {
     (void)count;
-    const cail_state_t &s = cail_global_state;
-    size_t one_max = s.oneshot_max ? s.oneshot_max
-                                   : (s.msg_small_threshold_set ? s.msg_small_threshold - 1
-                                                                : default_oneshot_max(dc->P));
-    if (bytes <= one_max) return CAIL_ALGO_ONE_SHOT;
-    if (nvls_min_ranks() > 0 && dc->P >= nvls_min_ranks() && cail_dev_nvls_ok(dc, dt, op) && bytes >= nvls_min_bytes())
-        return CAIL_ALGO_NVLS;
-    if (bytes >= ce_min_bytes()) return CAIL_ALGO_CE_TWO_SHOT;
-    return CAIL_ALGO_TWO_SHOT;
+    return pick_nvlink(dc->P, bytes, cail_dev_nvls_ok(dc, dt, op) != 0);
+}
+
+const char *cail_nvlink_auto_algorithm(int nranks, size_t bytes, MPI_Datatype datatype, MPI_Op op) {
+    if (nranks < 1 || !cail_type_supported(datatype) || !cail_op_supported(op)) return nullptr;
+    cail_load_config();
+    const cail_datatype_t dt = cail_mpi_type_to_dtype(datatype);
+    const cail_op_t o = cail_mpi_op_to_optype(op);
+    const bool pair = cail_global_state.nvls && cail::nvls_supported((int)o, (int)cail_elem_class(dt));
+    return cail_algo_name(pick_nvlink(nranks, bytes, pair));
 }
 
 int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *recvbuf, int count,
