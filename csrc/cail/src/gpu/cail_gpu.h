@@ -15,7 +15,11 @@
 extern "C" {
 #endif
 
+/* 1 if ptr is device (or managed) memory.  Makes the buffer's device current
+ * for the call, remembering the caller's; cail_gpu_restore_device() puts the
+ * caller's back when the call returns. */
 int cail_gpu_is_device_pointer(const void *ptr);
+void cail_gpu_restore_device(void);
 
 /* inout[i] = op(inout[i], in[i]) for i in [0, count) */
 int cail_gpu_reduce_local(const void *in, void *inout, size_t count, cail_datatype_t dtype,

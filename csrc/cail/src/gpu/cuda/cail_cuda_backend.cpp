@@ -30,6 +30,9 @@ bool cuda_present() {
     return g_cuda == 1;
 }
 
+// The caller's device while a call runs on its buffer's device (-1: none).
+thread_local int t_caller_device = -1;
+
 int current_device() {
     int d = 0;
     cudaGetDevice(&d);
@@ -73,9 +76,20 @@ int cail_gpu_is_device_pointer(const void *ptr) {
         return 0;
     }
     if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) return 0;
-    // run the call on the buffer's device
-    if (a.device >= 0 && a.device != current_device()) cudaSetDevice(a.device);
+    // run the call on the buffer's device; the caller's comes back at return
+    const int cur = current_device();
+    if (a.device >= 0 && a.device != cur) {
+        if (t_caller_device < 0) t_caller_device = cur;
+        cudaSetDevice(a.device);
+    }
     return 1;
+}
+
+void cail_gpu_restore_device(void) {
+    if (t_caller_device >= 0) {
+        cudaSetDevice(t_caller_device);
+        t_caller_device = -1;
+    }
 }
 
 int cail_gpu_reduce_local(const void *in, void *inout, size_t count, cail_datatype_t dtype,

@@ -38,6 +38,8 @@ int cail_gpu_is_device_pointer(const void *ptr) {
     return 0;
 }
 
+void cail_gpu_restore_device(void) {}
+
 int cail_gpu_reduce_local(const void *in, void *inout, size_t count, cail_datatype_t dtype,
                           cail_op_t op) {
     cail_elem_class_t ec = cail_elem_class(dtype);

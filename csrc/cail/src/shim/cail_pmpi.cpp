@@ -26,10 +26,10 @@ inline int passthrough(const void *s, void *r, int n, MPI_Datatype dt, MPI_Op op
 }
 }  // namespace
 
-extern "C" {
+namespace {
 
-int MPI_Allreduce(const void *sendbuf, void *recvbuf, int count, MPI_Datatype datatype, MPI_Op op,
-                  MPI_Comm comm) {
+int allreduce_filtered(const void *sendbuf, void *recvbuf, int count, MPI_Datatype datatype, MPI_Op op,
+                       MPI_Comm comm) {
     int rc;
     if (!cail_is_initialized()) {
         rc = cail_init(comm);
@@ -95,6 +95,18 @@ int MPI_Allreduce(const void *sendbuf, void *recvbuf, int count, MPI_Datatype da
                         cail_mpi_op_to_optype(op), np, cail_now_us() - t0);
     }
     return MPI_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+int MPI_Allreduce(const void *sendbuf, void *recvbuf, int count, MPI_Datatype datatype, MPI_Op op,
+                  MPI_Comm comm) {
+    const int rc = allreduce_filtered(sendbuf, recvbuf, count, datatype, op, comm);
+    // the call ran on its buffers' device; the caller keeps its own
+    cail_gpu_restore_device();
+    return rc;
 }
 
 int MPI_Finalize(void) {

@@ -36,6 +36,19 @@ def test_smoke_entry():
     assert "smoke ok" in r.stdout
 
 
+def test_call_keeps_the_callers_current_device():
+    # a buffer on cuda:1 while cuda:0 is current: the call runs on GPU 1 and
+    # hands GPU 0 back as the current device
+    need_gpus(2)
+    code = ("import cail_b200 as c, torch; torch.cuda.set_device(0); c.init();"
+            "x = torch.full((1 << 18,), 3.0, device='cuda:1'); c.ops.allreduce_(x);"
+            "torch.cuda.synchronize(1); d = torch.cuda.current_device();"
+            "ok = bool((x == 3.0).all()); c.finalize(); print('device', d, 'ok', ok)")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "device 0 ok True" in r.stdout, r.stdout + r.stderr
+
+
 def test_native_library_loaded_in_process():
     need_gpus(1)
     code = ("import cail_b200 as c, torch; c.init(); x=torch.ones(1<<20, device='cuda');"
