@@ -858,9 +858,10 @@ int run_oneshot_chunked(cail_dev_comm *dc, const char *src, char *dst, size_t co
 // result into every peer's output (ce_push); the three stages of successive
 // chunks overlap.  Chunks rotate through CAIL_CE_BUFFERS (2..4, default 4)
 // scratch buffers, and the pulls into a buffer wait for the fold that last
-// read it.  Only copy
-// engines touch NVLink: with both directions busy they move 773 GB/s per
-// direction on B200, against 704 for SM stores and 664 for SM loads.
+// read it.  Only copy engines touch NVLink: with both directions busy they
+// move 773 GB/s per direction between two B200s, against 704 for SM stores
+// and 664 for SM loads.  Each chunk costs 2(P-1) serial copies per engine,
+// so the path loses to the SM two-shot as P grows (350 vs 655 GB/s at 8).
 constexpr size_t kCeScratchMax = (size_t)512 << 20;
 
 int ce_buffers() {
