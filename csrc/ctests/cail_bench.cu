@@ -7,6 +7,8 @@
 //
 //   cail-mpirun -np N -x LD_PRELOAD=build/lib/libcail.so cail_bench \
 //       [-b min_bytes] [-e max_bytes] [-i iters] [-w warmup] [-d double] [--inplace]
+//   cail_bench --host [-b] [-e] [-i] [-w]   the same sweep on malloc'd host
+//       buffers (host-only build, CPU ranks; also runs without a GPU)
 //   cail_bench --stress [-i calls]    latency / stress workload: MPI_DOUBLE SUM,
 //       `calls` (default 10000) back-to-back calls at 32, 64, 128 and 256 KiB
 //       rotating over 64 distinct allocations with MPI_IN_PLACE on every other
@@ -113,7 +115,7 @@ static int run_stress(int rank, int P, int calls, algo_fn last) {
 int main(int argc, char **argv) {
     size_t minb = 32 << 10, maxb = 1 << 30;
     int iters = 100, warm = 20;
-    bool dbl = false, inplace = false, stress = false;
+    bool dbl = false, inplace = false, stress = false, host = false;
     for (int i = 1; i < argc; ++i) {
         std::string a = argv[i];
         if (a == "-b" && i + 1 < argc) minb = strtoull(argv[++i], nullptr, 10);
@@ -123,15 +125,18 @@ int main(int argc, char **argv) {
         else if (a == "-d") dbl = true;
         else if (a == "--inplace") inplace = true;
         else if (a == "--stress") stress = true;
+        else if (a == "--host") host = true;
     }
     MPI_Init(&argc, &argv);
     int rank, P;
     MPI_Comm_rank(MPI_COMM_WORLD, &rank);
     MPI_Comm_size(MPI_COMM_WORLD, &P);
     int ndev = 0;
-    cudaGetDeviceCount(&ndev);
-    const char *lr = getenv("CMPI_LOCAL_RANK");
-    cudaSetDevice((lr ? atoi(lr) : rank) % (ndev ? ndev : 1));
+    if (!host) {
+        cudaGetDeviceCount(&ndev);
+        const char *lr = getenv("CMPI_LOCAL_RANK");
+        cudaSetDevice((lr ? atoi(lr) : rank) % (ndev ? ndev : 1));
+    }
     algo_fn last = (algo_fn)dlsym(RTLD_DEFAULT, "cail_last_algorithm");
     if (stress) {
         int rc = run_stress(rank, P, iters == 100 ? 10000 : iters, last);
@@ -139,15 +144,23 @@ int main(int argc, char **argv) {
         return rc;
     }
     float *s = nullptr, *r = nullptr;
-    cudaMalloc(&s, maxb);
-    cudaMalloc(&r, maxb);
-    fill<<<1024, 256>>>(s, maxb / 4, (float)rank);
-    fill<<<1024, 256>>>(r, maxb / 4, (float)rank);
-    cudaDeviceSynchronize();
+    if (host) {
+        s = (float *)malloc(maxb);
+        r = (float *)malloc(maxb);
+        if (!s || !r) { MPI_Abort(MPI_COMM_WORLD, 1); }
+        for (size_t i = 0; i < maxb / 4; ++i) s[i] = r[i] = (float)rank + (float)(i % 1024) * 1e-3f;
+    } else {
+        cudaMalloc(&s, maxb);
+        cudaMalloc(&r, maxb);
+        fill<<<1024, 256>>>(s, maxb / 4, (float)rank);
+        fill<<<1024, 256>>>(r, maxb / 4, (float)rank);
+        cudaDeviceSynchronize();
+    }
     MPI_Datatype dt = dbl ? MPI_DOUBLE : MPI_FLOAT;
     int esz = dbl ? 8 : 4;
-    if (rank == 0) printf("# cail_bench np=%d iters=%d warmup=%d %s %s\nbytes,algo,p50_us,p99_us,mean_us,busbw_gbps\n",
-                          P, iters, warm, dbl ? "MPI_DOUBLE" : "MPI_FLOAT", inplace ? "in_place" : "separate");
+    if (rank == 0) printf("# cail_bench np=%d iters=%d warmup=%d %s %s %s\nbytes,algo,p50_us,p99_us,mean_us,busbw_gbps\n",
+                          P, iters, warm, dbl ? "MPI_DOUBLE" : "MPI_FLOAT", inplace ? "in_place" : "separate",
+                          host ? "host" : "device");
     std::vector<double> t(iters);
     for (size_t b = minb; b <= maxb; b *= 2) {
         int n = (int)(b / esz);
@@ -171,8 +184,13 @@ int main(int argc, char **argv) {
             printf("%zu,%s,%.2f,%.2f,%.2f,%.2f\n", b, last ? last() : "n/a", mx[0], mx[1], mx[2], bus);
         fflush(stdout);
     }
-    cudaFree(s);
-    cudaFree(r);
+    if (host) {
+        free(s);
+        free(r);
+    } else {
+        cudaFree(s);
+        cudaFree(r);
+    }
     MPI_Finalize();
     return 0;
 }
