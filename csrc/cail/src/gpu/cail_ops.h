@@ -31,11 +31,15 @@ struct Wrap {
     static CAIL_HD T add(T a, T b) { return a + b; }
     static CAIL_HD T mul(T a, T b) { return a * b; }
 };
+// Integers wrap: the arithmetic runs in an unsigned type at least as wide as
+// unsigned int, since 8- and 16-bit unsigned operands would otherwise be
+// promoted to (signed) int, where 65535 * 65535 overflows.
 template <typename T>
 struct Wrap<T, true> {
     using U = typename std::make_unsigned<T>::type;
-    static CAIL_HD T add(T a, T b) { return (T)(U)((U)a + (U)b); }
-    static CAIL_HD T mul(T a, T b) { return (T)(U)((U)a * (U)b); }
+    using W = typename std::conditional<(sizeof(U) < sizeof(unsigned)), unsigned, U>::type;
+    static CAIL_HD T add(T a, T b) { return (T)(U)((W)(U)a + (W)(U)b); }
+    static CAIL_HD T mul(T a, T b) { return (T)(U)((W)(U)a * (W)(U)b); }
 };
 
 template <int OP, typename T>

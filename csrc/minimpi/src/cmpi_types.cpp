@@ -68,11 +68,14 @@ struct Arith {
     static T add(T a, T b) { return a + b; }
     static T mul(T a, T b) { return a * b; }
 };
+// Wrapping arithmetic in an unsigned type no narrower than unsigned int (8-
+// and 16-bit unsigned operands would be promoted to signed int).
 template <typename T>
 struct Arith<T, true> {
     using U = typename Unsigned<T>::type;
-    static T add(T a, T b) { return (T)(U)((U)a + (U)b); }
-    static T mul(T a, T b) { return (T)(U)((U)a * (U)b); }
+    using W = typename std::conditional<(sizeof(U) < sizeof(unsigned)), unsigned, U>::type;
+    static T add(T a, T b) { return (T)(U)((W)(U)a + (W)(U)b); }
+    static T mul(T a, T b) { return (T)(U)((W)(U)a * (W)(U)b); }
 };
 
 template <typename T>

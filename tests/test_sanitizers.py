@@ -1,9 +1,10 @@
-"""The host path under AddressSanitizer with leak detection: a host-only build
-of minimpi, the interposer (linked in, as a link-time interposition) and the
-checks, compiled with -fsanitize=address.  Every rank must end with no
-sanitizer report, i.e. no invalid access and nothing left allocated after
-MPI_Finalize's teardown.  A deliberately leaking rank shows the check works
-under the launcher."""
+"""The host path under AddressSanitizer (with leak detection) and
+UndefinedBehaviorSanitizer: a host-only build of minimpi, the interposer
+(linked in, as a link-time interposition) and the checks, compiled with
+-fsanitize=address,undefined.  Every rank must end with no sanitizer report:
+no invalid access, no undefined arithmetic (e.g. 16-bit products promoted to
+signed int) and nothing left allocated after MPI_Finalize's teardown.  A
+deliberately leaking rank shows the check works under the launcher."""
 import os
 import shutil
 import subprocess
@@ -12,9 +13,9 @@ import pytest
 
 from conftest import ROOT
 
-ASAN = os.path.join(ROOT, "build-asan")
+ASAN = os.path.join(ROOT, "build-sanitize")
 CC, CXX = "/usr/bin/gcc", "/usr/bin/g++"
-ENV_ASAN = {"ASAN_OPTIONS": "detect_leaks=1:halt_on_error=1"}
+ENV_ASAN = {"ASAN_OPTIONS": "detect_leaks=1:halt_on_error=1", "UBSAN_OPTIONS": "print_stacktrace=1"}
 
 LEAK = r"""
 #include <mpi.h>
@@ -35,7 +36,8 @@ def _can_sanitize(tmp):
     src = os.path.join(tmp, "probe.c")
     with open(src, "w") as f:
         f.write("int main(void) { return 0; }\n")
-    r = subprocess.run([CC, "-fsanitize=address", src, "-o", os.path.join(tmp, "probe")], capture_output=True)
+    r = subprocess.run([CC, "-fsanitize=address,undefined", src, "-o", os.path.join(tmp, "probe")],
+                       capture_output=True)
     return r.returncode == 0
 
 
@@ -45,7 +47,8 @@ def asan_build(tmp_path_factory):
         pytest.skip("no AddressSanitizer runtime for the system compiler")
     if not os.path.exists(os.path.join(ASAN, "build.ninja")):
         r = subprocess.run(["cmake", "-S", ROOT, "-B", ASAN, "-G", "Ninja", "-DCAIL_HOST_PATH=ON",
-                            "-DCAIL_SANITIZE=address", f"-DCMAKE_C_COMPILER={CC}", f"-DCMAKE_CXX_COMPILER={CXX}"],
+                            "-DCAIL_SANITIZE=address,undefined", f"-DCMAKE_C_COMPILER={CC}",
+                            f"-DCMAKE_CXX_COMPILER={CXX}"],
                            capture_output=True, text=True, timeout=300)
         assert r.returncode == 0, r.stdout + r.stderr
     r = subprocess.run(["cmake", "--build", ASAN, "--target", "mpi", "cail-mpirun", "cail_check_linked"],
@@ -73,12 +76,12 @@ def _run(build, np, args, extra_env=None, timeout=600):
     (5, ["-m", "matrix", "-c", "1003"], {"CAIL_MIN_MSG_SIZE": "0", "CAIL_ALGO": "rabenseifner"}),
     (6, ["-m", "matrix", "-c", "1003"], {"CAIL_MIN_MSG_SIZE": "0", "CAIL_ALGO": "ring"}),
 ])
-def test_host_path_is_clean_under_asan(asan_build, np, mode, extra):
+def test_host_path_is_clean_under_sanitizers(asan_build, np, mode, extra):
     r = _run(asan_build, np, [os.path.join(asan_build, "bin", "cail_check_linked")] + mode, extra)
     out = r.stdout + r.stderr
     assert r.returncode == 0, out[-4000:]
     assert ", 0 failed" in r.stdout
-    assert "Sanitizer" not in out, out[-4000:]
+    assert "Sanitizer" not in out and "runtime error" not in out, out[-4000:]
 
 
 def test_leak_check_catches_a_leaking_rank(asan_build, tmp_path):
@@ -86,7 +89,8 @@ def test_leak_check_catches_a_leaking_rank(asan_build, tmp_path):
     src.write_text(LEAK)
     exe = tmp_path / "leak"
     lib = os.path.join(asan_build, "lib")
-    r = subprocess.run([CC, "-fsanitize=address", f"-I{os.path.join(ROOT, 'csrc', 'minimpi', 'include')}", str(src),
+    r = subprocess.run([CC, "-fsanitize=address,undefined", f"-I{os.path.join(ROOT, 'csrc', 'minimpi', 'include')}",
+                        str(src),
                         "-o", str(exe), f"-L{lib}", "-lmpi", f"-Wl,-rpath,{lib}"], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     r = _run(asan_build, 2, [str(exe)], timeout=120)
