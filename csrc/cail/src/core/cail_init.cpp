@@ -11,7 +11,9 @@
 //   CAIL_ALGO                 auto | recursive_doubling | ring | rabenseifner
 //                             | one_shot | two_shot | nvls
 // An invalid value prints "[cail ERROR] invalid X='v', using default".
+#include <ctype.h>
 #include <limits.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 #include <time.h>
@@ -55,6 +57,77 @@ bool parse_long(const char *name, const char *val, long lo, long hi, long *out) 
 const char *env_nonempty(const char *name) {
     const char *v = getenv(name);
     return (v && v[0] != '\0') ? v : nullptr;
+}
+
+// CAIL_TUNE_FILE: one line per rank count, "nranks=8 oneshot_max=262144
+// nvls_min=64M ce_min=512M" (any subset of the size keys; integers with an
+// optional K, M or G suffix; '#' starts a comment).  A bad line is reported
+// and ignored; a later line for the same nranks replaces an earlier one.
+constexpr int kMaxTune = 64;
+cail_tune_t g_tune[kMaxTune];
+int g_ntune = 0;
+
+bool parse_size(const char *v, long long *out) {
+    char *end = nullptr;
+    if (!isdigit((unsigned char)v[0])) return false;
+    long long x = strtoll(v, &end, 10);
+    long long mul = 1;
+    if (*end == 'K' || *end == 'k') mul = 1LL << 10, ++end;
+    else if (*end == 'M' || *end == 'm') mul = 1LL << 20, ++end;
+    else if (*end == 'G' || *end == 'g') mul = 1LL << 30, ++end;
+    if (*end != '\0' || x < 0 || x > (LLONG_MAX >> 30)) return false;
+    *out = x * mul;
+    return true;
+}
+
+void load_tune(const char *path) {
+    FILE *f = fopen(path, "r");
+    if (!f) {
+        CAIL_ERR("cannot open CAIL_TUNE_FILE '%s'", path);
+        return;
+    }
+    char line[512];
+    int lineno = 0;
+    while (fgets(line, sizeof line, f)) {
+        ++lineno;
+        if (char *h = strchr(line, '#')) *h = '\0';
+        cail_tune_t t = {0, -1, -1, -1};
+        bool bad = false, any = false;
+        char *save = nullptr;
+        for (char *tok = strtok_r(line, " \t\r\n", &save); tok && !bad; tok = strtok_r(nullptr, " \t\r\n", &save)) {
+            any = true;
+            char *eq = strchr(tok, '=');
+            if (!eq) { bad = true; break; }
+            *eq = '\0';
+            const char *key = tok, *val = eq + 1;
+            long long x = 0;
+            if (!parse_size(val, &x)) bad = true;
+            else if (!strcmp(key, "nranks")) {
+                if (x >= 1 && x <= INT_MAX) t.nranks = (int)x;
+                else bad = true;
+            }
+            else if (!strcmp(key, "oneshot_max")) t.oneshot_max = x;
+            else if (!strcmp(key, "nvls_min")) t.nvls_min = x;
+            else if (!strcmp(key, "ce_min")) t.ce_min = x;
+            else bad = true;
+        }
+        if (!any) continue;
+        if (bad || t.nranks < 1) {
+            CAIL_ERR("CAIL_TUNE_FILE '%s' line %d: expected nranks=<n> and oneshot_max=, nvls_min=, ce_min= "
+                     "sizes; line ignored", path, lineno);
+            continue;
+        }
+        int i = 0;
+        while (i < g_ntune && g_tune[i].nranks != t.nranks) ++i;
+        if (i == kMaxTune) {
+            CAIL_ERR("CAIL_TUNE_FILE '%s' line %d: more than %d rank counts; line ignored", path, lineno, kMaxTune);
+            continue;
+        }
+        g_tune[i] = t;
+        if (i == g_ntune) ++g_ntune;
+    }
+    fclose(f);
+    CAIL_DBG("CAIL_TUNE_FILE '%s': %d rank count(s)", path, g_ntune);
 }
 
 bool g_stream_sync_set = false;  // cail_set_stream_sync() overrides the environment
@@ -159,6 +232,13 @@ void cail_load_config(void) {
         s.trace = fopen(e, "a");
         if (!s.trace) CAIL_ERR("cannot open CAIL_TRACE file '%s'", e);
     }
+    if ((e = env_nonempty(CAIL_ENV_TUNE_FILE))) load_tune(e);
+}
+
+const cail_tune_t *cail_tune_for(int nranks) {
+    for (int i = 0; i < g_ntune; ++i)
+        if (g_tune[i].nranks == nranks) return &g_tune[i];
+    return nullptr;
 }
 
 int cail_init(MPI_Comm comm) {

@@ -88,6 +88,20 @@ enum {
 extern "C" {
 #endif
 
+/* One line of CAIL_TUNE_FILE: measured crossovers for NVLink communicators of
+ * `nranks` ranks, in bytes; -1 where the line gives none.  The environment
+ * variables of the same meaning (CAIL_ONESHOT_MAX, CAIL_MSG_SMALL_THRESHOLD,
+ * CAIL_NVLS_MIN_RANKS / CAIL_NVLS_MIN, CAIL_CE_MIN) take precedence. */
+typedef struct {
+    int nranks;
+    long long oneshot_max; /* one_shot up to this size */
+    long long nvls_min;    /* nvls from this size (where multimem can reduce the pair) */
+    long long ce_min;      /* ce_two_shot from this size */
+} cail_tune_t;
+
+/* The CAIL_TUNE_FILE line for `nranks`, or NULL. */
+const cail_tune_t *cail_tune_for(int nranks);
+
 extern cail_state_t cail_global_state;
 extern cail_stats_t cail_counters;
 extern int cail_last_algo;

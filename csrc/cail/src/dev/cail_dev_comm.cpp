@@ -481,10 +481,14 @@ bool nvls_step(cail_dev_comm *dc, bool ok, CUresult r, const char *what) {
 int nvls_min_ranks();
 
 // The multicast region (a 512 MiB granule per GPU) is created only where it
-// can be used: CAIL_ALGO=nvls, or auto mode with CAIL_NVLS_MIN_RANKS <= P.
+// can be used: CAIL_ALGO=nvls, or auto mode with CAIL_NVLS_MIN_RANKS <= P or
+// a CAIL_TUNE_FILE line for P that gives nvls_min.
 bool nvls_wanted(int P) {
     if (!cail_global_state.nvls || P < 2) return false;
-    return cail_global_state.force_algo == CAIL_ALGO_NVLS || (nvls_min_ranks() > 0 && P >= nvls_min_ranks());
+    if (cail_global_state.force_algo == CAIL_ALGO_NVLS) return true;
+    if (nvls_min_ranks() > 0) return P >= nvls_min_ranks();
+    const cail_tune_t *t = cail_tune_for(P);
+    return t && t->nvls_min >= 0;
 }
 
 void nvls_setup(cail_dev_comm *dc, bool all_capable) {
@@ -1134,8 +1138,10 @@ int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
     return check_status(dc, "nvls");
 }
 
+// Built-in one_shot / two_shot crossover (measured on B200 at 2 to 8 ranks:
+// one_shot is ahead up to 512 KiB).  CAIL_TUNE_FILE lines replace it per
+// rank count.
 size_t default_oneshot_max(int P) {
-    // measured crossovers are loaded from CAIL_TUNE_FILE when given
     (void)P;
     return 512 << 10;
 }
@@ -1157,7 +1163,7 @@ size_t nvls_min_bytes() {
 }
 
 // Auto mode hands messages of at least CAIL_CE_MIN bytes to the
-// copy-engine two-shot.
+// copy-engine two-shot (~0 when unset).
 size_t ce_min_bytes() {
     static const size_t v = [] {
         const char *e = getenv("CAIL_CE_MIN");
@@ -1177,15 +1183,28 @@ int nvls_min_ranks() {
 // Auto mode on an NVLink communicator of P ranks; nvls_pair: NVLS is set up
 // and multimem can reduce the call's (type, op).  Depends only on its
 // arguments and the environment.
+// Precedence for each crossover: its environment variable, then the
+// CAIL_TUNE_FILE line for P, then the built-in default.
 int pick_nvlink(int P, size_t bytes, bool nvls_pair) {
     const cail_state_t &s = cail_global_state;
+    const cail_tune_t *t = cail_tune_for(P);
     size_t one_max = s.oneshot_max ? s.oneshot_max
-                                   : (s.msg_small_threshold_set ? s.msg_small_threshold - 1
-                                                                : default_oneshot_max(P));
+                     : s.msg_small_threshold_set ? s.msg_small_threshold - 1
+                     : (t && t->oneshot_max >= 0) ? (size_t)t->oneshot_max
+                                                  : default_oneshot_max(P);
     if (bytes <= one_max) return CAIL_ALGO_ONE_SHOT;
-    if (nvls_min_ranks() > 0 && P >= nvls_min_ranks() && nvls_pair && bytes >= nvls_min_bytes())
-        return CAIL_ALGO_NVLS;
-    if (bytes >= ce_min_bytes()) return CAIL_ALGO_CE_TWO_SHOT;
+    if (nvls_pair) {
+        if (nvls_min_ranks() > 0) {
+            if (P >= nvls_min_ranks() && bytes >= nvls_min_bytes()) return CAIL_ALGO_NVLS;
+        } else if (t && t->nvls_min >= 0 && bytes >= (size_t)t->nvls_min) {
+            return CAIL_ALGO_NVLS;
+        }
+    }
+    if (ce_min_bytes() != ~(size_t)0) {
+        if (bytes >= ce_min_bytes()) return CAIL_ALGO_CE_TWO_SHOT;
+    } else if (t && t->ce_min >= 0 && bytes >= (size_t)t->ce_min) {
+        return CAIL_ALGO_CE_TWO_SHOT;
+    }
     return CAIL_ALGO_TWO_SHOT;
 }
 
