@@ -7,7 +7,7 @@
 // compared with PMPI_Allreduce of the same inputs (integers bit-exact,
 // floats bit-exact or within a reassociation tolerance, see --tol).
 //
-//   cail_check -m basic|matrix|edge|config1|stress [-c count] [-d] [-a algo]
+//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest [-c count] [-d] [-a algo]
 //              [-p] [-r reps] [--bits]
 //     -d      device buffers (cudaMalloc) instead of malloc
 //     -a      sets CAIL_ALGO before the first MPI_Allreduce
@@ -78,19 +78,56 @@ const char *last_algo() {
 }
 
 // ---- buffers that may live on the device
+// Every buffer sits between two 256-byte canary zones (the user region stays
+// 256-byte aligned, as cudaMalloc's would be).  Reading a result back and
+// releasing a buffer check that no call wrote outside [p, p + bytes);
+// a damaged zone counts as a failure in the next report and in the summary.
+constexpr size_t kGuard = 256;
+constexpr unsigned char kCanary = 0xA5;
+int g_canary_bad = 0;
+
 struct Buf {
     size_t bytes = 0;
+    char *base = nullptr;
     void *p = nullptr;
     explicit Buf(size_t b) : bytes(b) {
+        const size_t total = b + 2 * kGuard;
+        std::vector<unsigned char> fillv(total, kCanary);
         if (g_dev) {
-            if (cudaMalloc(&p, b ? b : 16) != cudaSuccess) { fprintf(stderr, "cudaMalloc failed\n"); MPI_Abort(MPI_COMM_WORLD, 2); }
+            if (cudaMalloc((void **)&base, total) != cudaSuccess) { fprintf(stderr, "cudaMalloc failed\n"); MPI_Abort(MPI_COMM_WORLD, 2); }
+            cudaMemcpy(base, fillv.data(), total, cudaMemcpyHostToDevice);
         } else {
-            p = malloc(b ? b : 16);
+            base = (char *)malloc(total);
+            memcpy(base, fillv.data(), total);
         }
+        p = base + kGuard;
     }
-    ~Buf() { if (g_dev) cudaFree(p); else free(p); }
+    ~Buf() {
+        check_guards();
+        if (g_dev) cudaFree(base); else free(base);
+    }
     void put(const void *h) { if (g_dev) cudaMemcpy(p, h, bytes, cudaMemcpyHostToDevice); else memcpy(p, h, bytes); }
-    void get(void *h) const { if (g_dev) cudaMemcpy(h, p, bytes, cudaMemcpyDeviceToHost); else memcpy(h, p, bytes); }
+    void get(void *h) const {
+        if (g_dev) cudaMemcpy(h, p, bytes, cudaMemcpyDeviceToHost); else memcpy(h, p, bytes);
+        check_guards();
+    }
+    void check_guards() const {
+        unsigned char z[2 * kGuard];
+        if (g_dev) {
+            cudaMemcpy(z, base, kGuard, cudaMemcpyDeviceToHost);
+            cudaMemcpy(z + kGuard, base + kGuard + bytes, kGuard, cudaMemcpyDeviceToHost);
+        } else {
+            memcpy(z, base, kGuard);
+            memcpy(z + kGuard, base + kGuard + bytes, kGuard);
+        }
+        for (size_t i = 0; i < 2 * kGuard; ++i)
+            if (z[i] != kCanary) {
+                if (g_canary_bad++ == 0)
+                    fprintf(stderr, "rank %d: canary byte %s the buffer overwritten (%zu bytes buffer)\n", g_rank,
+                            i < kGuard ? "before" : "after", bytes);
+                break;
+            }
+    }
 };
 
 // Seeded, position-dependent inputs.  Integers in [-8, 8] (SUM/MAX/MIN) or
@@ -131,6 +168,11 @@ bool compare(const std::vector<char> &got, const std::vector<char> &want, const 
 }
 
 void report(bool ok, const std::string &what) {
+    static int canary_seen = 0;
+    if (g_canary_bad != canary_seen) {  // a zone was damaged since the last report
+        canary_seen = g_canary_bad;
+        ok = false;
+    }
     int mine = ok ? 1 : 0, all = 0;
     PMPI_Allreduce(&mine, &all, 1, MPI_INT, MPI_MIN, MPI_COMM_WORLD);
     if (all) g_pass++; else g_fail++;
@@ -213,6 +255,19 @@ void mode_config3(double tol) {
                 bool ok = check_one(t, o, c, false, seed++, tol);
                 report(ok, std::string(t.name) + " x " + o.name + " count=" + std::to_string(c));
             }
+}
+
+// Positive control of the canary zones: writes one byte just past a buffer
+// (inside its own guard zone, so nothing outside the allocation is touched)
+// and expects the check to notice.
+void mode_canary_selftest() {
+    Buf b(1024);
+    const unsigned char x = 0;
+    if (g_dev) cudaMemcpy((char *)b.p + 1024, &x, 1, cudaMemcpyHostToDevice);
+    else memcpy((char *)b.p + 1024, &x, 1);
+    std::vector<char> h(1024);
+    b.get(h.data());
+    report(g_canary_bad == 0, "canary zones intact after a deliberate one-byte overrun");
 }
 
 void mode_edge() {
@@ -445,7 +500,9 @@ int main(int argc, char **argv) {
     else if (mode == "config1") mode_config1(tol);
     else if (mode == "stress") mode_stress(count ? count : 4096, reps, nbuf, tol);
     else if (mode == "leave") mode_leave(count ? count : 65536);
+    else if (mode == "canary_selftest") mode_canary_selftest();
     else { fprintf(stderr, "unknown mode %s\n", mode.c_str()); MPI_Abort(MPI_COMM_WORLD, 2); }
+    if (mode != "leave") report(g_canary_bad == 0, "canary zones around every buffer intact");
     if (g_rank == 0) printf("=== Results: %d passed, %d failed ===\n", g_pass, g_fail);
     MPI_Finalize();
     return g_fail ? 1 : 0;

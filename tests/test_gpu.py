@@ -36,6 +36,14 @@ def test_smoke_entry():
     assert "smoke ok" in r.stdout
 
 
+def test_canary_zones_catch_an_overrun_on_the_device():
+    # the guard zones around device buffers are checked the same way
+    need_gpus(1)
+    r = mpirun(1, ["cail_check", "-m", "canary_selftest", "-d"], preload="cuda", timeout=300)
+    assert r.returncode != 0
+    assert "FAIL: canary zones intact after a deliberate one-byte overrun" in r.stdout
+
+
 def test_call_keeps_the_callers_current_device():
     # a buffer on cuda:1 while cuda:0 is current: the call runs on GPU 1 and
     # hands GPU 0 back as the current device

@@ -141,6 +141,15 @@ def test_forced_device_algorithm_on_host_build_warns(algo):
     assert f"[cail WARN] forced {algo} needs the CUDA build, falling back to PMPI" in r.stderr
 
 
+def test_canary_zones_catch_an_overrun():
+    # every cail_check buffer sits between guard zones checked after each
+    # call; the self-test overruns one buffer by a byte and must fail
+    r = mpirun(2, ["cail_check", "-m", "canary_selftest"])
+    assert r.returncode != 0
+    assert "FAIL: canary zones intact after a deliberate one-byte overrun" in r.stdout
+    assert "canary byte after the buffer overwritten" in r.stderr
+
+
 # ---------------------------------------------------------------- logging / env
 def test_unsupported_type_warns_and_warn_zero_silences():
     r = mpirun(2, ["cail_check", "-m", "edge"])
