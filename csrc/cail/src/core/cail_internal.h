@@ -70,6 +70,7 @@ typedef struct cail_state {
     int stream_sync;             /* order device work after the legacy stream */
     int profile;                 /* CAIL_PROFILE: host-side phase timers */
     int stream_ordered;          /* one-shot calls complete in stream order, not on the host */
+    int nvtx;                    /* CAIL_NVTX: an NVTX range per call (CUDA build) */
 } cail_state_t;
 
 /* Opt-in host-side phase timers (CAIL_PROFILE=1), averaged per call and

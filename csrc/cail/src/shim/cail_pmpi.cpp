@@ -14,6 +14,10 @@
 #include "../dev/cail_dev.h"
 #include "../gpu/cail_gpu.h"
 
+#ifndef CAIL_HOST_PATH
+#include <nvtx3/nvToolsExt.h>  // header-only; calls are no-ops without a profiler attached
+#endif
+
 extern "C" int cail_allreduce_dispatch_ex(const void *sendbuf, void *recvbuf, int count,
                                           MPI_Datatype datatype, MPI_Op op, MPI_Comm comm,
                                           int *may_fallback);
@@ -103,9 +107,30 @@ extern "C" {
 
 int MPI_Allreduce(const void *sendbuf, void *recvbuf, int count, MPI_Datatype datatype, MPI_Op op,
                   MPI_Comm comm) {
+#ifndef CAIL_HOST_PATH
+    // CAIL_NVTX=1: one range per call, named with the message size, and a
+    // mark with the algorithm that ran (or "pmpi")
+    cail_load_config();
+    const bool nvtx = cail_global_state.nvtx != 0;
+    if (nvtx) {
+        int ts = 0;
+        PMPI_Type_size(datatype, &ts);
+        char msg[96];
+        snprintf(msg, sizeof msg, "cail MPI_Allreduce %lld B", (long long)count * ts);
+        nvtxRangePushA(msg);
+    }
+#endif
     const int rc = allreduce_filtered(sendbuf, recvbuf, count, datatype, op, comm);
     // the call ran on its buffers' device; the caller keeps its own
     cail_gpu_restore_device();
+#ifndef CAIL_HOST_PATH
+    if (nvtx) {
+        char msg[64];
+        snprintf(msg, sizeof msg, "cail algorithm=%s", cail_last_algorithm());
+        nvtxMarkA(msg);
+        nvtxRangePop();
+    }
+#endif
     return rc;
 }
 

@@ -141,6 +141,13 @@ def test_forced_device_algorithm_on_host_build_warns(algo):
     assert f"[cail WARN] forced {algo} needs the CUDA build, falling back to PMPI" in r.stderr
 
 
+def test_nvtx_ranges_are_harmless_without_a_profiler():
+    # CAIL_NVTX=1 wraps every call of the CUDA build in an NVTX range; with no
+    # profiler attached the calls are no-ops (host buffers: passthrough here)
+    r = mpirun(2, ["cail_check", "-m", "basic"], preload="cuda", env={"CAIL_NVTX": "1"})
+    assert ok(r), r.stdout + r.stderr
+
+
 def test_canary_zones_catch_an_overrun():
     # every cail_check buffer sits between guard zones checked after each
     # call; the self-test overruns one buffer by a byte and must fail
