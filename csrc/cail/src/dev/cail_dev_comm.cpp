@@ -136,6 +136,10 @@ struct BufDesc {
     int32_t pad;
 };
 
+// arrive / depart hold the call sequence number; a rank that failed sets
+// kXErr as well, so its peers stop waiting and report the error too.
+constexpr uint64_t kXErr = 1ull << 63;
+
 struct alignas(128) XSlot {
     std::atomic<uint64_t> arrive;
     char pad0[56];
@@ -977,25 +981,54 @@ int ce_body(cail_dev_comm *dc, const char *const *srcs, char *const *dsts, size_
     return check_status(dc, "ce_two_shot");
 }
 
+// 1 if a peer published kXErr in its arrive (depart) word for this call.
+bool peer_failed(const cail_dev_comm *dc, bool depart) {
+    for (int q = 0; q < dc->P; ++q) {
+        const std::atomic<uint64_t> &a = depart ? dc->xs[q].depart : dc->xs[q].arrive;
+        if (a.load(std::memory_order_acquire) & kXErr) return true;
+    }
+    return false;
+}
+
+// Host-side fault injection (tests only): CAIL_FI_TWOSHOT_FAIL=<rank> makes
+// that rank's import of its peers' buffers fail, as a failing
+// cudaIpcOpenMemHandle would.
+int fi_twoshot_fail_rank() {
+    static const int v = [] {
+        const char *e = getenv("CAIL_FI_TWOSHOT_FAIL");
+        return e && *e ? atoi(e) : -1;
+    }();
+    return v;
+}
+
+// A rank that fails between the host barriers still takes part in both, with
+// kXErr set, so no peer waits forever and no peer reports a result whose
+// slice of the failed rank was never reduced.
 int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec,
                 bool ce = false) {
     XSlot &me = dc->xs[dc->rank];
     // Peers read this rank's buffers as soon as it arrives, so its pending
     // legacy-stream writes must have landed first.
+    bool pre_ok = true;
     if (cail_global_state.stream_sync && cudaEventSynchronize(dc->legacy_ev) != cudaSuccess) {
         CAIL_ERR("two_shot: waiting for the legacy stream failed");
-        return MPI_ERR_OTHER;
+        pre_ok = false;
     }
     describe(dc, src, &me.send);
     describe(dc, dst, &me.recv);
     uint64_t seq = ++dc->xseq;
-    me.arrive.store(seq, std::memory_order_release);
+    me.arrive.store(pre_ok ? seq : (seq | kXErr), std::memory_order_release);
     double th = cail_global_state.profile ? cail_now_us() : 0.0;
     int rc = host_wait(dc, false, seq);
     th = cail_prof_mark(CAIL_PH_HOSTSYNC, th);
     if (rc != MPI_SUCCESS) return rc;
     bool all_ok = true;
     for (int q = 0; q < dc->P; ++q) all_ok = all_ok && dc->xs[q].send.ok && dc->xs[q].recv.ok;
+    if (!pre_ok || peer_failed(dc, false)) {
+        if (pre_ok) CAIL_ERR("two_shot: a peer failed before the exchange; not launching");
+        rc = MPI_ERR_OTHER;
+        goto depart;
+    }
     if (!all_ok) {
         // some rank's buffer cannot be exported: every rank sees the same
         // descriptors and takes the copy-in path instead
@@ -1017,9 +1050,13 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
             a.dst[q] = import_buf(dc, q, dc->xs[q].recv);
             if (!a.src[q] || !a.dst[q]) bad = true;
         }
+        if (dc->rank == fi_twoshot_fail_rank()) {
+            CAIL_ERR("two_shot: injected import failure (CAIL_FI_TWOSHOT_FAIL)");
+            bad = true;
+        }
         if (bad) {
-            dc->broken = true;
-            return MPI_ERR_OTHER;
+            rc = MPI_ERR_OTHER;
+            goto depart;
         }
         if (ce) {
             rc = ce_body(dc, a.src, a.dst, count, esz, op, ec);
@@ -1075,10 +1112,15 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
 depart:
     // depart: peers may only return (and reuse their buffers) once every
     // rank's kernel has finished reading and writing them
-    me.depart.store(seq, std::memory_order_release);
+    me.depart.store(rc == MPI_SUCCESS ? seq : (seq | kXErr), std::memory_order_release);
     th = cail_global_state.profile ? cail_now_us() : 0.0;
     int rc2 = host_wait(dc, true, seq);
     cail_prof_mark(CAIL_PH_HOSTSYNC, th);
+    if (rc == MPI_SUCCESS && rc2 == MPI_SUCCESS && peer_failed(dc, true)) {
+        CAIL_ERR("two_shot: a peer failed during the call; the result is incomplete");
+        rc2 = MPI_ERR_OTHER;
+    }
+    if (rc != MPI_SUCCESS || rc2 != MPI_SUCCESS) dc->broken = true;
     return rc != MPI_SUCCESS ? rc : rc2;
 }
 

@@ -7,7 +7,8 @@
 // compared with PMPI_Allreduce of the same inputs (integers bit-exact,
 // floats bit-exact or within a reassociation tolerance, see --tol).
 //
-//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest [-c count] [-d] [-a algo]
+//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest|expect_error
+//              [-c count] [-d] [-a algo]
 //              [-p] [-r reps] [--bits]
 //     -d      device buffers (cudaMalloc) instead of malloc
 //     -a      sets CAIL_ALGO before the first MPI_Allreduce
@@ -257,6 +258,22 @@ void mode_config3(double tol) {
             }
 }
 
+// With a failure injected on one rank (CAIL_FI_TWOSHOT_FAIL), a large call
+// must return an error on every rank (none may hang or report success), and
+// so must the next call on the same communicator.
+void mode_expect_error(int count) {
+    Buf s(count * sizeof(float)), r(count * sizeof(float));
+    std::vector<float> h(count, 1.0f);
+    s.put(h.data());
+    double t0 = MPI_Wtime();
+    int rc1 = MPI_Allreduce(s.p, r.p, count, MPI_FLOAT, MPI_SUM, MPI_COMM_WORLD);
+    int rc2 = MPI_Allreduce(s.p, r.p, count, MPI_FLOAT, MPI_SUM, MPI_COMM_WORLD);
+    double dt = MPI_Wtime() - t0;
+    report(rc1 != MPI_SUCCESS, "failed call returns an error on every rank");
+    report(rc2 != MPI_SUCCESS, "the next call on the broken communicator returns an error too");
+    report(dt < 30.0, "both calls return within 30 s");
+}
+
 // Positive control of the canary zones: writes one byte just past a buffer
 // (inside its own guard zone, so nothing outside the allocation is touched)
 // and expects the check to notice.
@@ -501,6 +518,7 @@ int main(int argc, char **argv) {
     else if (mode == "stress") mode_stress(count ? count : 4096, reps, nbuf, tol);
     else if (mode == "leave") mode_leave(count ? count : 65536);
     else if (mode == "canary_selftest") mode_canary_selftest();
+    else if (mode == "expect_error") mode_expect_error(count ? count : (1 << 20));
     else { fprintf(stderr, "unknown mode %s\n", mode.c_str()); MPI_Abort(MPI_COMM_WORLD, 2); }
     if (mode != "leave") report(g_canary_bad == 0, "canary zones around every buffer intact");
     if (g_rank == 0) printf("=== Results: %d passed, %d failed ===\n", g_pass, g_fail);

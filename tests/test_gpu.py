@@ -182,6 +182,21 @@ def test_stream_ordered_small_messages_bit_exact():
 
 
 @pytest.mark.multigpu
+def test_two_shot_failure_on_one_rank_reaches_every_rank():
+    """A failure injected on the host of rank 1 (its import of the peers'
+    buffers fails, as a failing cudaIpcOpenMemHandle would) must end the
+    two-shot call with an error on every rank: rank 1 still passes both host
+    barriers with an error bit, so rank 0 neither waits forever nor returns
+    a result whose slice 1 was never reduced.  No GPU fault is involved."""
+    need_gpus(2)
+    r = mpirun(2, ["cail_check", "-m", "expect_error", "-d"], preload="cuda",
+               env={"CAIL_ALGO": "two_shot", "CAIL_FI_TWOSHOT_FAIL": "1", "CAIL_NVLS": "0"}, timeout=300)
+    assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+    assert "injected import failure" in r.stderr
+    assert "a peer failed during the call" in r.stderr
+
+
+@pytest.mark.multigpu
 def test_rank_leaving_between_steps_is_detected():
     need_gpus(2)
     r = mpirun(2, ["cail_check", "-m", "leave", "-d"], preload="cuda",
