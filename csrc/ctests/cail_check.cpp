@@ -7,7 +7,7 @@
 // compared with PMPI_Allreduce of the same inputs (integers bit-exact,
 // floats bit-exact or within a reassociation tolerance, see --tol).
 //
-//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest|expect_error
+//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest|expect_error|memkinds
 //              [-c count] [-d] [-a algo]
 //              [-p] [-r reps] [--bits]
 //     -d      device buffers (cudaMalloc) instead of malloc
@@ -256,6 +256,46 @@ void mode_config3(double tol) {
                 bool ok = check_one(t, o, c, false, seed++, tol);
                 report(ok, std::string(t.name) + " x " + o.name + " count=" + std::to_string(c));
             }
+}
+
+// Device-pointer detection over the four kinds of memory an application may
+// hand in: cudaMalloc and managed memory run on cail's device path, pinned
+// (cudaMallocHost) and malloc'd memory pass through to PMPI_Allreduce.
+// Every call must produce the PMPI result.
+void mode_memkinds() {
+    const char *names[4] = {"cudaMalloc", "cudaMallocManaged", "cudaMallocHost", "malloc"};
+    for (int kind = 0; kind < 4; ++kind) {
+        for (size_t count : {(size_t)16384, (size_t)262144}) {  // 64 KiB and 1 MiB of floats
+            const size_t bytes = count * sizeof(float);
+            float *s = nullptr, *r = nullptr;
+            bool alloc_ok = true;
+            if (kind == 0) alloc_ok = cudaMalloc(&s, bytes) == cudaSuccess && cudaMalloc(&r, bytes) == cudaSuccess;
+            if (kind == 1) alloc_ok = cudaMallocManaged(&s, bytes) == cudaSuccess && cudaMallocManaged(&r, bytes) == cudaSuccess;
+            if (kind == 2) alloc_ok = cudaMallocHost(&s, bytes) == cudaSuccess && cudaMallocHost(&r, bytes) == cudaSuccess;
+            if (kind == 3) { s = (float *)malloc(bytes); r = (float *)malloc(bytes); alloc_ok = s && r; }
+            std::vector<float> h(count), want(count), got(count);
+            for (size_t i = 0; i < count; ++i) h[i] = (float)((i * 7 + (size_t)g_rank * 13) % 101) - 50.0f;
+            bool ok = alloc_ok;
+            if (ok) {
+                if (kind < 2) cudaMemcpy(s, h.data(), bytes, cudaMemcpyDefault);
+                else memcpy(s, h.data(), bytes);
+                PMPI_Allreduce(h.data(), want.data(), (int)count, MPI_FLOAT, MPI_SUM, MPI_COMM_WORLD);
+                ok = MPI_Allreduce(s, r, (int)count, MPI_FLOAT, MPI_SUM, MPI_COMM_WORLD) == MPI_SUCCESS;
+                if (kind < 2) cudaMemcpy(got.data(), r, bytes, cudaMemcpyDefault);
+                else memcpy(got.data(), r, bytes);
+                ok = ok && memcmp(got.data(), want.data(), bytes) == 0;
+                const std::string algo = last_algo();
+                const bool device_kind = kind < 2;
+                // an interposer without cail_last_algorithm reports "n/a"
+                if (algo != "n/a") ok = ok && ((algo == "pmpi") != device_kind);
+            }
+            report(ok, std::string(names[kind]) + " buffers, " + std::to_string(bytes) + " bytes, " +
+                           (kind < 2 ? "device path" : "PMPI passthrough"));
+            if (kind == 0 || kind == 1) { cudaFree(s); cudaFree(r); }
+            if (kind == 2) { cudaFreeHost(s); cudaFreeHost(r); }
+            if (kind == 3) { free(s); free(r); }
+        }
+    }
 }
 
 // With a failure injected on one rank (CAIL_FI_TWOSHOT_FAIL), a large call
@@ -519,6 +559,7 @@ int main(int argc, char **argv) {
     else if (mode == "leave") mode_leave(count ? count : 65536);
     else if (mode == "canary_selftest") mode_canary_selftest();
     else if (mode == "expect_error") mode_expect_error(count ? count : (1 << 20));
+    else if (mode == "memkinds") mode_memkinds();
     else { fprintf(stderr, "unknown mode %s\n", mode.c_str()); MPI_Abort(MPI_COMM_WORLD, 2); }
     if (mode != "leave") report(g_canary_bad == 0, "canary zones around every buffer intact");
     if (g_rank == 0) printf("=== Results: %d passed, %d failed ===\n", g_pass, g_fail);

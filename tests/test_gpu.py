@@ -36,6 +36,14 @@ def test_smoke_entry():
     assert "smoke ok" in r.stdout
 
 
+def test_device_pointer_detection_over_memory_kinds():
+    # cudaMalloc and managed buffers take the device path, pinned host and
+    # malloc'd buffers pass through to PMPI; all give the PMPI result
+    need_gpus(1)
+    r = mpirun(1, ["cail_check", "-m", "memkinds"], preload="cuda", timeout=300)
+    assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+
+
 def test_canary_zones_catch_an_overrun_on_the_device():
     # the guard zones around device buffers are checked the same way
     need_gpus(1)
