@@ -159,3 +159,103 @@ def test_dead_peer_detected(probe):
                     "CMPI_FI_EXIT_CODE": "0"})
     assert r.returncode != 0
     assert "exited without MPI_Finalize" in r.stderr
+
+
+PROBE2 = r"""
+#include <mpi.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+int main(int argc, char **argv) {
+    int flag = -1, provided = -1, bad = 0;
+    MPI_Initialized(&flag);
+    bad |= flag != 0;
+    MPI_Init_thread(&argc, &argv, MPI_THREAD_FUNNELED, &provided);
+    MPI_Initialized(&flag);
+    bad |= flag != 1 || provided < MPI_THREAD_SINGLE;
+    int q = -1;
+    MPI_Query_thread(&q);
+    bad |= q != provided;
+    int r, p;
+    MPI_Comm_rank(MPI_COMM_WORLD, &r);
+    MPI_Comm_size(MPI_COMM_WORLD, &p);
+    /* non-blocking ring in both directions, completed with Waitall */
+    int n = 1 << 18;
+    int *s0 = malloc(n * sizeof(int)), *s1 = malloc(n * sizeof(int));
+    int *r0 = malloc(n * sizeof(int)), *r1 = malloc(n * sizeof(int));
+    for (int i = 0; i < n; i++) { s0[i] = r * 7 + i; s1[i] = -(r * 7 + i); }
+    int right = (r + 1) % p, left = (r + p - 1) % p;
+    MPI_Request req[4];
+    MPI_Status sts[4];
+    MPI_Irecv(r0, n, MPI_INT, left, 1, MPI_COMM_WORLD, &req[0]);
+    MPI_Irecv(r1, n, MPI_INT, right, 2, MPI_COMM_WORLD, &req[1]);
+    MPI_Isend(s0, n, MPI_INT, right, 1, MPI_COMM_WORLD, &req[2]);
+    MPI_Isend(s1, n, MPI_INT, left, 2, MPI_COMM_WORLD, &req[3]);
+    MPI_Waitall(4, req, sts);
+    for (int i = 0; i < n; i += 997) bad |= r0[i] != left * 7 + i || r1[i] != -(right * 7 + i);
+    bad |= sts[0].MPI_SOURCE != left || sts[1].MPI_SOURCE != right;
+    for (int i = 0; i < 4; i++) bad |= req[i] != MPI_REQUEST_NULL;
+    /* Test until complete, then Wait on the nulled request */
+    int tok = r, got = -1, done = 0;
+    MPI_Request a, b;
+    MPI_Irecv(&got, 1, MPI_INT, left, 3, MPI_COMM_WORLD, &a);
+    MPI_Isend(&tok, 1, MPI_INT, right, 3, MPI_COMM_WORLD, &b);
+    while (!done) MPI_Test(&a, &done, MPI_STATUS_IGNORE);
+    MPI_Wait(&b, MPI_STATUS_IGNORE);
+    bad |= got != left;
+    /* gather to a non-zero root on a duplicated communicator */
+    MPI_Comm dup;
+    MPI_Comm_dup(MPI_COMM_WORLD, &dup);
+    int root = p - 1, *all = malloc(p * sizeof(int));
+    int mine = 100 + r;
+    MPI_Gather(&mine, 1, MPI_INT, all, 1, MPI_INT, root, dup);
+    if (r == root) for (int i = 0; i < p; i++) bad |= all[i] != 100 + i;
+    MPI_Comm_free(&dup);
+    /* extents, error strings, clocks, processor name */
+    MPI_Datatype three;
+    MPI_Type_contiguous(3, MPI_DOUBLE, &three);
+    MPI_Type_commit(&three);
+    MPI_Aint lb = -1, ext = -1;
+    MPI_Type_get_extent(three, &lb, &ext);
+    bad |= lb != 0 || ext != 24;
+    MPI_Type_free(&three);
+    char msg[MPI_MAX_ERROR_STRING];
+    int len = 0;
+    MPI_Error_string(MPI_ERR_COUNT, msg, &len);
+    bad |= len <= 0 || (int)strlen(msg) != len;
+    double t0 = MPI_Wtime(), t1 = MPI_Wtime();
+    bad |= t1 < t0 || MPI_Wtick() <= 0.0;
+    char host[MPI_MAX_PROCESSOR_NAME];
+    MPI_Get_processor_name(host, &len);
+    bad |= len <= 0;
+    int any = 0;
+    MPI_Allreduce(&bad, &any, 1, MPI_INT, MPI_LOR, MPI_COMM_WORLD);
+    MPI_Finalized(&flag);
+    any |= flag != 0;
+    if (r == 0) printf("minimpi probe2 %s p=%d\n", any ? "FAIL" : "OK", p);
+    MPI_Finalize();
+    MPI_Finalized(&flag);
+    if (r == 0 && flag != 1) printf("Finalized flag not set\n");
+    return any || flag != 1;
+}
+"""
+
+
+@pytest.fixture(scope="module")
+def probe2(build, tmp_path_factory):
+    d = tmp_path_factory.mktemp("mpi2")
+    src = d / "probe2.c"
+    src.write_text(PROBE2)
+    exe = d / "probe2"
+    inc = os.path.join(ROOT, "csrc", "minimpi", "include")
+    subprocess.run(["gcc", "-O1", f"-I{inc}", str(src), "-o", str(exe), f"-L{LIB}", "-lmpi",
+                    f"-Wl,-rpath,{LIB}"], check=True)
+    return str(exe)
+
+
+@pytest.mark.parametrize("np", [1, 2, 3, 5])
+def test_minimpi_nonblocking_gather_dup_and_queries(probe2, np):
+    r = subprocess.run([os.path.join(BIN, "cail-mpirun"), "-np", str(np), probe2], capture_output=True,
+                       text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert f"minimpi probe2 OK p={np}" in r.stdout
