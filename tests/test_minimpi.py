@@ -79,6 +79,7 @@ int main(int argc, char **argv) {
     int any = 0;
     MPI_Allreduce(&bad, &any, 1, MPI_INT, MPI_LOR, MPI_COMM_WORLD);
     if (r == 0) printf("minimpi probe %s p=%d\n", any ? "FAIL" : "OK", p);
+    free(a); free(b); free(all);
     MPI_Finalize();
     return any;
 }
@@ -233,6 +234,7 @@ int main(int argc, char **argv) {
     MPI_Finalized(&flag);
     any |= flag != 0;
     if (r == 0) printf("minimpi probe2 %s p=%d\n", any ? "FAIL" : "OK", p);
+    free(s0); free(s1); free(r0); free(r1); free(all);
     MPI_Finalize();
     MPI_Finalized(&flag);
     if (r == 0 && flag != 1) printf("Finalized flag not set\n");

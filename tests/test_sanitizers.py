@@ -96,3 +96,24 @@ def test_leak_check_catches_a_leaking_rank(asan_build, tmp_path):
     r = _run(asan_build, 2, [str(exe)], timeout=120)
     assert r.returncode != 0
     assert "LeakSanitizer: detected memory leaks" in r.stderr and "12345 byte" in r.stderr
+
+
+@pytest.mark.parametrize("which", ["PROBE", "PROBE2"])
+def test_minimpi_probes_are_clean_under_sanitizers(asan_build, tmp_path, which):
+    # minimpi's point-to-point, non-blocking, collective and communicator code
+    # under ASan + UBSan (the probe programs of test_minimpi.py)
+    import test_minimpi
+
+    src = tmp_path / "probe.c"
+    src.write_text(getattr(test_minimpi, which))
+    exe = tmp_path / "probe"
+    lib = os.path.join(asan_build, "lib")
+    r = subprocess.run([CC, "-O1", "-fsanitize=address,undefined",
+                        f"-I{os.path.join(ROOT, 'csrc', 'minimpi', 'include')}", str(src), "-o", str(exe),
+                        f"-L{lib}", "-lmpi", f"-Wl,-rpath,{lib}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = _run(asan_build, 3, [str(exe)], timeout=300)
+    out = r.stdout + r.stderr
+    assert r.returncode == 0, out[-4000:]
+    assert " OK p=3" in r.stdout
+    assert "Sanitizer" not in out and "runtime error" not in out, out[-4000:]
