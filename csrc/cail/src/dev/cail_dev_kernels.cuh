@@ -105,6 +105,11 @@ cudaError_t launch_twoshot(int op, int ec, const TwoShotArgs &a, int blocks, int
                            cudaStream_t s);
 cudaError_t launch_nvls(int op, int ec, const NvlsArgs &a, int blocks, int threads, cudaStream_t s);
 cudaError_t launch_fold(int op, int ec, const FoldArgs &a, int blocks, int threads, cudaStream_t s);
+// Device copy through TMA bulk copies (experimental, single-GPU harness only);
+// src and dst must share their alignment modulo 16.  *status gets 1 when a
+// wait ran out after spin_limit polls.
+cudaError_t launch_bulk_copy(char *dst, const char *src, size_t bytes, int blocks, unsigned long long spin_limit,
+                             int *status, cudaStream_t s);
 // 1 if the NVLS kernel exists for (op, ec).
 int nvls_supported(int op, int ec);
 // Element-wise local reduction io = op(io, in) (PMPI algorithm path).

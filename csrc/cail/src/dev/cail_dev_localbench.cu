@@ -6,7 +6,9 @@
 // the one-shot kernel pushes into P scratch areas and folds P slots, with
 // its peers' arrival flags set in advance (so it never waits).  The fold
 // kernel of the copy-engine two-shot runs on P local sources as it does in
-// production (there it is local already).  The
+// production (there it is local already).  Kernel 3 is the experimental
+// TMA bulk-copy kernel (a one-rank allreduce is a copy), checked against its
+// source after timing.  The
 // instruction stream is the production one; only NVLink is replaced by
 // local HBM.  This is the case a profiler can capture on one GPU.
 #include <cuda_runtime.h>
@@ -18,6 +20,21 @@
 #include "cail_dev_kernels.cuh"
 
 namespace {
+
+// Counts 16-byte words that differ between a and b (n16 words).
+__global__ void count_diff(const uint4 *a, const uint4 *b, size_t n16, unsigned long long *bad) {
+    unsigned long long mine = 0;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
+        const uint4 x = a[i], y = b[i];
+        mine += (x.x != y.x) | (x.y != y.y) | (x.z != y.z) | (x.w != y.w);
+    }
+    if (mine) atomicAdd(bad, mine);
+}
+
+__global__ void fill_pattern(uint32_t *p, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        p[i] = (uint32_t)(i * 2654435761u) ^ 0x5bd1e995u;
+}
 
 struct Bufs {
     std::vector<void *> ptrs;
@@ -35,7 +52,8 @@ struct Bufs {
 
 }  // namespace
 
-// kernel: 0 = one_shot, 1 = two_shot, 2 = fold (P sources of `bytes`).  Runs `iters` launches of a float SUM
+// kernel: 0 = one_shot, 1 = two_shot, 2 = fold (P sources of `bytes`),
+// 3 = bulk copy of `bytes` (P ignored; returns -2 if the copy differs).  Runs `iters` launches of a float SUM
 // over `bytes` bytes per rank with P emulated ranks (2..8) and writes the
 // mean time per launch in milliseconds to *ms.  Returns 0 or -1.
 extern "C" int cail_bench_kernel_local(int kernel, int P, size_t bytes, int iters, float *ms) {
@@ -86,6 +104,28 @@ extern "C" int cail_bench_kernel_local(int kernel, int P, size_t bytes, int iter
         cudaEventRecord(e0, s);
         for (int i = 0; i < iters; ++i) cail::launch_oneshot(CAIL_SUM, CAIL_EC_F32, a, blocks, 512, s);
         cudaEventRecord(e1, s);
+    } else if (kernel == 3) {
+        char *src = b.get(bytes + 16), *dst = b.get(bytes + 16);
+        int *bst = (int *)b.get(sizeof(int));
+        unsigned long long *bad = (unsigned long long *)b.get(sizeof(unsigned long long));
+        if (!src || !dst || !bst || !bad || bytes % 16) { rc = -1; goto out; }
+        fill_pattern<<<1024, 256, 0, s>>>((uint32_t *)src, bytes / 4);
+        const unsigned long long limit = 1ull << 24;  // try_wait polls before giving up
+        int blocks = sms;
+        if (cail::launch_bulk_copy(dst, src, bytes, blocks, limit, bst, s) != cudaSuccess) { rc = -1; goto out; }
+        cudaEventRecord(e0, s);
+        for (int i = 0; i < iters; ++i) cail::launch_bulk_copy(dst, src, bytes, blocks, limit, bst, s);
+        cudaEventRecord(e1, s);
+        count_diff<<<1024, 256, 0, s>>>((const uint4 *)src, (const uint4 *)dst, bytes / 16, bad);
+        unsigned long long h_bad = 0;
+        int h_st = 0;
+        if (cudaStreamSynchronize(s) != cudaSuccess ||
+            cudaMemcpy(&h_bad, bad, sizeof(h_bad), cudaMemcpyDeviceToHost) != cudaSuccess ||
+            cudaMemcpy(&h_st, bst, sizeof(h_st), cudaMemcpyDeviceToHost) != cudaSuccess) {
+            rc = -1;
+            goto out;
+        }
+        if (h_bad || h_st) rc = -2;
     } else if (kernel == 2) {
         cail::FoldArgs a;
         memset(&a, 0, sizeof(a));
