@@ -141,3 +141,21 @@ def test_tune_analysis_places_crossovers_from_sweeps():
     assert tune.tune_line(8, one, two, nvls, two_big) == "nranks=8 oneshot_max=524288 nvls_min=268435456"
     # never winning leaves the key out (the library keeps its default)
     assert tune.tune_line(2, two, one) == "nranks=2"
+
+
+def test_info_tool_prints_the_policy_table(tmp_path):
+    f = tmp_path / "cail.tune"
+    f.write_text("nranks=8 oneshot_max=256K nvls_min=256M\n")
+    e = {k: v for k, v in os.environ.items() if not k.startswith("CAIL_")}
+    e["CAIL_TUNE_FILE"] = str(f)
+    r = subprocess.run([sys.executable, "-m", "cail_b200.info", "--ranks", "2,8"], cwd=ROOT, env=e,
+                       capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    lines = r.stdout.splitlines()
+    assert lines[0].startswith("cail 0.1.0")
+    assert f"CAIL_TUNE_FILE={f}" in r.stdout
+    row2 = next(l for l in lines if l.startswith("2 ")).split()
+    row8 = next(l for l in lines if l.startswith("8 ")).split()
+    # columns: 32K 256K 512K 1M 16M 256M 1G
+    assert row2[1:] == ["one_shot", "one_shot", "one_shot", "two_shot", "two_shot", "two_shot", "two_shot"]
+    assert row8[1:] == ["one_shot", "one_shot", "two_shot", "two_shot", "two_shot", "nvls", "nvls"]
