@@ -22,6 +22,11 @@ all_reduce; --impl pmpi runs the MPI's own PMPI_Allreduce (no interposer).
 busbw = 2 (P-1)/P * bytes / t (nccl-tests convention).  With one GPU that
 factor is 0, so the N=1 value is algbw = bytes / t of the single-rank call
 (a device copy through cail's kernels).
+
+--workload ddp runs the data-parallel GPT-2-medium step instead (tokens/s and
+exposed communication): gradients in 25 MB buckets all-reduced through the
+interposer (ours, reference, pmpi), or PyTorch's DistributedDataParallel
+over NCCL with the same bucket size (--impl nccl).
 """
 from __future__ import annotations
 
@@ -150,6 +155,75 @@ def run_ddp(args, rank: int, world: int, local: int, comm: "Comm") -> dict:
     }
 
 
+def run_ddp_nccl(args, rank: int, world: int, local: int, comm: "Comm") -> dict:
+    """The same GPT-2-medium step under PyTorch's DistributedDataParallel over
+    NCCL (25 MB buckets, gradients as bucket views): the NCCL baseline of the
+    data-parallel workload.  Compute-only time runs the loop under no_sync()."""
+    import contextlib
+
+    import torch
+    from torch.nn.parallel import DistributedDataParallel as DDP
+
+    from cail_b200.models import GPT2, GPT2Config
+
+    cfg = GPT2Config.medium()
+    mb, seq = args.micro_batch, cfg.n_ctx
+    torch.manual_seed(0)
+    model = GPT2(cfg).cuda()
+    net = DDP(model, device_ids=[local], bucket_cap_mb=25, gradient_as_bucket_view=True) if world > 1 else model
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    g = torch.Generator().manual_seed(4242 + rank)
+    host_x = torch.randint(0, cfg.vocab, (mb, seq), generator=g).pin_memory()
+    host_y = torch.randint(0, cfg.vocab, (mb, seq), generator=g).pin_memory()
+    x = torch.empty_like(host_x, device="cuda")
+    y = torch.empty_like(host_y, device="cuda")
+
+    def step(sync: bool):
+        opt.zero_grad(set_to_none=False)
+        x.copy_(host_x, non_blocking=True)
+        y.copy_(host_y, non_blocking=True)
+        ctx = contextlib.nullcontext() if (sync or world == 1) else net.no_sync()
+        with ctx:
+            loss = net(x, y)
+            loss.backward()
+        opt.step()
+        return loss.item()  # device->host read of the step's result
+
+    def timed(sync: bool) -> float:
+        comm.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step(sync)
+        torch.cuda.synchronize()
+        return comm.max((time.perf_counter() - t0) / args.steps)
+
+    for _ in range(args.warmup):
+        step(True)
+    t_compute = timed(False)
+    t_full = timed(True)
+    tokens = world * mb * seq
+    return {
+        "metric": "DDP GPT-2-medium training throughput (tokens/s, fp32 grads, 25 MB buckets)",
+        "value": round(tokens / t_full, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_full * 1e3, 3),
+        "compute_only_ms_per_step": round(t_compute * 1e3, 3),
+        "exposed_comm_ms": round((t_full - t_compute) * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "dtype": "fp32",
+        "data": "synthetic token ids uniform over the vocabulary; random-init weights",
+        "config": {"model": "GPT-2 medium (24L, d1024, 16H, MLP 4096, vocab 50257)", "global_batch": world * mb,
+                   "seq_len": seq, "parallelism": f"dp{world}", "buckets": "torch DDP, bucket_cap_mb=25",
+                   "params": model.num_params()},
+        "impl": "nccl",
+    }
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", default="allreduce", choices=["allreduce", "ddp"])
@@ -223,8 +297,13 @@ def main() -> None:
     P = world
     if args.workload == "ddp":
         if args.impl == "nccl":
-            log("bench: the ddp workload runs through MPI_Allreduce (ours, reference or pmpi)")
-            sys.exit(2)
+            out = run_ddp_nccl(args, rank, world, local, comm)
+            if rank == 0:
+                print(json.dumps(out), flush=True)
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
+            return
         out = run_ddp(args, rank, world, local, comm)
         if rank == 0:
             print(json.dumps(out), flush=True)
