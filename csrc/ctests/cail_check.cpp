@@ -7,7 +7,7 @@
 // compared with PMPI_Allreduce of the same inputs (integers bit-exact,
 // floats bit-exact or within a reassociation tolerance, see --tol).
 //
-//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest|expect_error|memkinds
+//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest|expect_error|memkinds|nan
 //              [-c count] [-d] [-a algo]
 //              [-p] [-r reps] [--bits]
 //     -d      device buffers (cudaMalloc) instead of malloc
@@ -27,6 +27,8 @@
 #include <string.h>
 #include <unistd.h>
 
+#include <cmath>
+#include <limits>
 #include <random>
 #include <string>
 #include <vector>
@@ -256,6 +258,52 @@ void mode_config3(double tol) {
                 bool ok = check_one(t, o, c, false, seed++, tol);
                 report(ok, std::string(t.name) + " x " + o.name + " count=" + std::to_string(c));
             }
+}
+
+// MAX / MIN on floats holding NaN and infinities.  The NVLink kernels fold in
+// rank order with acc = (acc > x) ? acc : x (MIN with <), like the PMPI
+// oracle, so the results must be bit-identical to PMPI's (NaN payloads
+// included).  Device buffers only: the host algorithms (recursive doubling,
+// ring, Rabenseifner) combine pairs in orders that differ between ranks, and
+// with a NaN, max(NaN, 1) != max(1, NaN), so there the ranks may disagree
+// (as with the reference's host algorithms).
+void mode_nan() {
+    if (!g_dev) {
+        report(true, "NaN/Inf MAX/MIN (device buffers only; nothing to check)");
+        return;
+    }
+    const float qnan = std::numeric_limits<float>::quiet_NaN(), inf = std::numeric_limits<float>::infinity();
+    const double dnan = std::numeric_limits<double>::quiet_NaN(), dinf = std::numeric_limits<double>::infinity();
+    for (size_t count : {(size_t)100003, (size_t)1000003}) {  // one-shot and two-shot sizes
+        for (int dbl = 0; dbl < 2; ++dbl) {
+            for (MPI_Op op : {MPI_MAX, MPI_MIN}) {
+                const size_t esz = dbl ? 8 : 4;
+                std::vector<char> h(count * esz), want(count * esz), got(count * esz);
+                std::mt19937_64 rng(77 + (uint64_t)g_rank);
+                for (size_t i = 0; i < count; ++i) {
+                    double v = std::normal_distribution<double>(0, 1)(rng);
+                    if (i % 7 == (size_t)(g_rank % 7)) v = dbl ? dnan : (double)qnan;
+                    if (g_rank == 0 && i % 11 == 0) v = dinf;
+                    if (g_rank == g_size - 1 && i % 13 == 0) v = -dinf;
+                    if (dbl) memcpy(h.data() + i * 8, &v, 8);
+                    else { float f = std::isnan(v) ? qnan : (std::isinf(v) ? (v > 0 ? inf : -inf) : (float)v); memcpy(h.data() + i * 4, &f, 4); }
+                }
+                MPI_Datatype dt = dbl ? MPI_DOUBLE : MPI_FLOAT;
+                PMPI_Allreduce(h.data(), want.data(), (int)count, dt, op, MPI_COMM_WORLD);
+                for (int ip = 0; ip < 2; ++ip) {
+                    Buf s(count * esz), r(count * esz);
+                    s.put(h.data());
+                    r.put(h.data());
+                    int rc = MPI_Allreduce(ip ? MPI_IN_PLACE : s.p, r.p, (int)count, dt, op, MPI_COMM_WORLD);
+                    r.get(got.data());
+                    report(rc == MPI_SUCCESS && memcmp(got.data(), want.data(), count * esz) == 0,
+                           std::string(ip ? "MPI_IN_PLACE " : "") + (dbl ? "DOUBLE " : "FLOAT ") +
+                               (op == MPI_MAX ? "MAX" : "MIN") + " with NaN/Inf count=" + std::to_string(count) +
+                               " bit-identical to PMPI");
+                }
+            }
+        }
+    }
 }
 
 // Device-pointer detection over the four kinds of memory an application may
@@ -560,6 +608,7 @@ int main(int argc, char **argv) {
     else if (mode == "canary_selftest") mode_canary_selftest();
     else if (mode == "expect_error") mode_expect_error(count ? count : (1 << 20));
     else if (mode == "memkinds") mode_memkinds();
+    else if (mode == "nan") mode_nan();
     else { fprintf(stderr, "unknown mode %s\n", mode.c_str()); MPI_Abort(MPI_COMM_WORLD, 2); }
     if (mode != "leave") report(g_canary_bad == 0, "canary zones around every buffer intact");
     if (g_rank == 0) printf("=== Results: %d passed, %d failed ===\n", g_pass, g_fail);

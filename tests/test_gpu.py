@@ -173,6 +173,17 @@ def test_registration_cache_stress():
 
 
 @pytest.mark.multigpu
+def test_nan_and_inf_max_min_bit_identical_to_pmpi():
+    """Float/double MAX and MIN over data holding NaN and +-Inf, one-shot and
+    two-shot sizes, separate and in place: the rank-order fold of the NVLink
+    kernels gives PMPI's result bit for bit."""
+    need_gpus(2)
+    for np in nranks():
+        r = mpirun(np, ["cail_check", "-m", "nan", "-d"], preload="cuda", timeout=900)
+        assert ok(r), f"np={np}\n" + r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.multigpu
 def test_stream_ordered_small_messages_bit_exact():
     """CAIL_STREAM_ORDERED=1: one-shot calls return once queued and the legacy
     stream waits for them; results read back through the legacy stream must
