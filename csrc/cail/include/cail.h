@@ -14,6 +14,7 @@
 #define CAIL_H
 
 #include <mpi.h>
+#include <stddef.h>
 
 #define CAIL_VERSION_MAJOR 0
 #define CAIL_VERSION_MINOR 1
@@ -27,15 +28,18 @@ extern "C" {
 const char *cail_version(void);
 
 /* Name of the algorithm that ran the last intercepted MPI_Allreduce of this
- * process ("one_shot", "two_shot", "nvls", "recursive_doubling", "ring",
- * "rabenseifner", "pmpi" for a passthrough, "none" before the first call). */
+ * process ("one_shot", "two_shot", "nvls", "ce_two_shot",
+ * "recursive_doubling", "ring", "rabenseifner", "pmpi" for a passthrough,
+ * "none" before the first call). */
 const char *cail_last_algorithm(void);
 
 /* Counters since initialisation. */
 typedef struct cail_stats {
     unsigned long long calls;          /* MPI_Allreduce calls seen */
     unsigned long long passthrough;    /* calls forwarded to PMPI_Allreduce */
-    unsigned long long by_algo[8];     /* indexed by cail_algo_t + 1 (auto=0 unused) */
+    unsigned long long by_algo[8];     /* calls per algorithm, index 1 + (0 recursive_doubling, 1 ring,
+                                          2 rabenseifner, 3 one_shot, 4 two_shot, 5 nvls,
+                                          6 ce_two_shot); index 0 unused */
     unsigned long long bytes;          /* payload bytes reduced by cail algorithms */
     unsigned long long reg_hits;       /* registration cache hits (peer buffers) */
     unsigned long long reg_misses;     /* registration cache misses (IPC opens) */
@@ -74,8 +78,8 @@ int cail_set_stream_ordered(int mode);
 /* The algorithm auto mode picks for an intercepted device-buffer call of
  * `bytes` bytes on an NVLink communicator of `nranks` ranks, under this
  * process' environment (CAIL_ONESHOT_MAX, CAIL_MSG_SMALL_THRESHOLD,
- * CAIL_NVLS_MIN_RANKS, CAIL_NVLS_MIN, CAIL_CE_MIN, CAIL_NVLS), assuming an
- * NVSwitch fabric with multicast.  NULL for an unsupported type or op.  Needs
+ * CAIL_TUNE_FILE, CAIL_NVLS_MIN_RANKS, CAIL_NVLS_MIN, CAIL_CE_MIN,
+ * CAIL_NVLS), assuming an NVSwitch fabric with multicast.  NULL for an unsupported type or op.  Needs
  * no MPI_Init: for checking a tuning before a job. */
 const char *cail_nvlink_auto_algorithm(int nranks, size_t bytes, MPI_Datatype datatype, MPI_Op op);
 
