@@ -8,7 +8,6 @@ import os
 import subprocess
 import sys
 
-import pytest
 
 from conftest import LIB, ROOT
 
