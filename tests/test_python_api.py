@@ -80,3 +80,32 @@ def test_bench_reference_arm_reports_unavailable_without_build(tmp_path):
     r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr
     assert '"unavailable"' in r.stdout and '"impl": "reference"' in r.stdout
+
+
+def test_max_min_nan_semantics_match_pmpi_reduce_local():
+    """cail's reduction template (shared by the host backend and the device
+    kernels) and minimpi's PMPI_Reduce_local agree bit for bit on MAX/MIN
+    over NaN and +-Inf, in both operand orders."""
+    import ctypes
+
+    import numpy as np
+
+    from cail_b200 import _lib
+
+    mpi = ctypes.CDLL(os.path.join(ROOT, "build", "lib", "libmpi.so"), mode=ctypes.RTLD_GLOBAL)
+    host = ctypes.CDLL(os.path.join(ROOT, "build", "lib", "libcail_host.so"))
+    vals = [float("nan"), float("inf"), float("-inf"), 0.0, -0.0, 1.5, -2.25]
+    a = np.array([x for x in vals for _ in vals], dtype=np.float32)
+    b = np.array([y for _ in vals for y in vals], dtype=np.float32)
+    # cail_types.h: dtype FLOAT = 3, DOUBLE = 4; op MAX = 2, MIN = 3
+    for dt_np, cail_dt, mpi_dt in ((np.float32, 3, "MPI_FLOAT"), (np.float64, 4, "MPI_DOUBLE")):
+        for cail_op, mpi_op in ((2, "MPI_MAX"), (3, "MPI_MIN")):
+            for x, y in ((a, b), (b, a)):
+                x, y = x.astype(dt_np), y.astype(dt_np)
+                io1, io2 = y.copy(), y.copy()
+                rc1 = host.cail_gpu_reduce_local(x.ctypes.data_as(ctypes.c_void_p), io1.ctypes.data_as(ctypes.c_void_p),
+                                                 ctypes.c_size_t(len(x)), cail_dt, cail_op)
+                rc2 = mpi.PMPI_Reduce_local(x.ctypes.data_as(ctypes.c_void_p), io2.ctypes.data_as(ctypes.c_void_p),
+                                            len(x), _lib.H[mpi_dt], _lib.H[mpi_op])
+                assert rc1 == 0 and rc2 == 0
+                assert io1.tobytes() == io2.tobytes(), (mpi_dt, mpi_op)
