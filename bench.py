@@ -282,15 +282,14 @@ def main() -> None:
         cail_b200.init(impl)
         comm = Comm(args.impl, cail_b200.rank(), cail_b200.world_size())
         H = _lib.H
-        from cail_b200.ops import ext
-
-        # MPI_Allreduce of the loaded library (ours or the reference) through
-        # the cail_torch extension: one pybind call, GIL released
-        ar = ext.get().allreduce
+        # MPI_Allreduce of the loaded library (ours, the reference or the
+        # MPI's own) called through ctypes, which releases the GIL; both arms
+        # take this same call path and load no Python extension of this repo
+        mpi_allreduce = _lib.loaded().cail.MPI_Allreduce
         dt, op, cw = H["MPI_FLOAT"], H["MPI_SUM"], H["MPI_COMM_WORLD"]
 
         def allreduce(src, dst):
-            rc = ar(src, dst, dt, op, cw)
+            rc = mpi_allreduce(src.data_ptr(), dst.data_ptr(), src.numel(), dt, op, cw)
             if rc != 0:
                 raise RuntimeError(f"MPI_Allreduce returned {rc}")
 
@@ -349,16 +348,43 @@ def main() -> None:
         import cail_b200
         algo = cail_b200.last_algorithm()
 
+    # ---------------- result check: every rank regenerates all P inputs from
+    # their seeds and folds them in rank order in fp32 (the oracle); the
+    # NVLink kernels fold in the same order, so floats must match bit for bit
+    def rank_order_fold() -> "torch.Tensor":
+        g = torch.Generator(device=dev)
+        acc = None
+        for r in range(P):
+            g.manual_seed(1234 + r)
+            x = torch.randn(count, device=dev, generator=g)
+            acc = x if acc is None else acc.add_(x)
+            del x
+        return acc
+
+    expect = rank_order_fold()
+    mismatches = comm.max(float((expect != recv).sum().item()))
+    max_err = comm.max(float((expect - recv).abs().max().item()))
+    del expect
+    if mismatches == 0:
+        check = "bit_exact"
+    else:
+        check = {"mismatches": int(mismatches), "max_abs_err": max_err,
+                 "note": "NCCL reduces in its own order" if args.impl == "nccl" else "differs from the rank-order fold"}
+
     # ---------------- end to end through the public API, host data
     e2e = None
     if not args.no_e2e:
+        if args.impl == "nccl":
+            public = allreduce
+        else:
+            from cail_b200.ops import allreduce as public  # the tensor API over MPI_Allreduce
         h_in = torch.empty(count, dtype=torch.float32, pin_memory=True)
         h_in.copy_(send.cpu())
         h_out = torch.empty(count, dtype=torch.float32, pin_memory=True)
         for _ in range(2):
             send.copy_(h_in, non_blocking=True)
             torch.cuda.synchronize()
-            allreduce(send, recv)
+            public(send, recv)
             h_out.copy_(recv, non_blocking=True)
             torch.cuda.synchronize()
         comm.barrier()
@@ -367,12 +393,13 @@ def main() -> None:
         for _ in range(args.steps):
             send.copy_(h_in, non_blocking=True)
             torch.cuda.synchronize()
-            allreduce(send, recv)
+            public(send, recv)
             h_out.copy_(recv, non_blocking=True)
             torch.cuda.synchronize()
         t_e2e = comm.max((time.perf_counter() - t0) / args.steps)
         e2e = {"value": busbw(args.bytes, t_e2e, P), "unit": "GB/s", "ms_per_step": t_e2e * 1e3,
-               "h2d_bytes_per_step": count * 4, "d2h_bytes_per_step": count * 4}
+               "h2d_bytes_per_step": count * 4, "d2h_bytes_per_step": count * 4,
+               "api": "torch.distributed.all_reduce" if args.impl == "nccl" else "cail_b200.ops.allreduce"}
         del h_in, h_out
 
     # ---------------- sweep
@@ -382,7 +409,7 @@ def main() -> None:
         while nbytes <= hi:
             n = nbytes // 4
             s, r = send[:n], recv[:n]
-            iters = args.sweep_iters if nbytes <= (128 << 20) else max(10, args.sweep_iters // 5)
+            iters = args.sweep_iters
             for _ in range(args.sweep_warmup):
                 allreduce(s, r)
             comm.barrier()
@@ -398,7 +425,7 @@ def main() -> None:
             p99 = comm.max(sorted(ts)[min(len(ts) - 1, int(math.ceil(0.99 * len(ts))) - 1)])
             mean = comm.max(sum(ts) / len(ts))
             row = {"bytes": nbytes, "busbw": round(busbw(nbytes, mean, P), 2), "p50_us": round(p50 * 1e6, 2),
-                   "p99_us": round(p99 * 1e6, 2)}
+                   "p99_us": round(p99 * 1e6, 2), "iters": iters}
             if args.impl == "ours":
                 import cail_b200
                 row["algo"] = cail_b200.last_algorithm()
@@ -450,6 +477,7 @@ def main() -> None:
         "clocks": clock_summary,
         "e2e": e2e,
         "gpu_launches": (l1 - l0) if (l0 is not None and l1 is not None) else None,
+        "check": check,
         "algorithm": algo,
         "sweep": sweep,
         "sweep_stream_ordered": sweep_ordered,

@@ -85,7 +85,7 @@ def set_stream_ordered(on: bool) -> Optional[bool]:
 
 class Stats(ctypes.Structure):
     _fields_ = [("calls", ctypes.c_ulonglong), ("passthrough", ctypes.c_ulonglong),
-                ("by_algo", ctypes.c_ulonglong * 8), ("bytes", ctypes.c_ulonglong),
+                ("by_algo", ctypes.c_ulonglong * 12), ("bytes", ctypes.c_ulonglong),
                 ("reg_hits", ctypes.c_ulonglong), ("reg_misses", ctypes.c_ulonglong),
                 ("device_errors", ctypes.c_ulonglong), ("launches", ctypes.c_ulonglong)]
 

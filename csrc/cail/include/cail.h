@@ -28,7 +28,8 @@ extern "C" {
 const char *cail_version(void);
 
 /* Name of the algorithm that ran the last intercepted MPI_Allreduce of this
- * process ("one_shot", "two_shot", "nvls", "ce_two_shot",
+ * process ("one_shot", "two_shot", "nvls", "ce_two_shot", "copy" (a one-rank
+ * communicator on device buffers),
  * "recursive_doubling", "ring", "rabenseifner", "pmpi" for a passthrough,
  * "none" before the first call). */
 const char *cail_last_algorithm(void);
@@ -37,9 +38,9 @@ const char *cail_last_algorithm(void);
 typedef struct cail_stats {
     unsigned long long calls;          /* MPI_Allreduce calls seen */
     unsigned long long passthrough;    /* calls forwarded to PMPI_Allreduce */
-    unsigned long long by_algo[8];     /* calls per algorithm, index 1 + (0 recursive_doubling, 1 ring,
+    unsigned long long by_algo[12];    /* calls per algorithm, index 1 + (0 recursive_doubling, 1 ring,
                                           2 rabenseifner, 3 one_shot, 4 two_shot, 5 nvls,
-                                          6 ce_two_shot); index 0 unused */
+                                          6 ce_two_shot, 7 copy); index 0 and 9..11 unused */
     unsigned long long bytes;          /* payload bytes reduced by cail algorithms */
     unsigned long long reg_hits;       /* registration cache hits (peer buffers) */
     unsigned long long reg_misses;     /* registration cache misses (IPC opens) */

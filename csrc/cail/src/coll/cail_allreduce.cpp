@@ -18,6 +18,7 @@
 //     msg < threshold -> recursive doubling, else Rabenseifner.
 #include "../core/cail_internal.h"
 #include "../dev/cail_dev.h"
+#include "../gpu/cail_gpu.h"
 #include "cail_p2p_algos.h"
 
 namespace {
@@ -107,6 +108,19 @@ extern "C" int cail_allreduce_dispatch_ex(const void *sendbuf, void *recvbuf, in
         count_algo(forced, msg);
         return a.fn(sendbuf, recvbuf, count, datatype, op, comm);
     }
+
+    // ---- one rank: the result is the input.  The reference's three
+    // algorithms copy sendbuf to recvbuf and return when P == 1
+    // (cail_allreduce_recursive_doubling.c:52-58 there); here the copy runs
+    // without any communicator setup, and an in-place call does nothing.
+#ifndef CAIL_HOST_PATH
+    if (nprocs == 1) {
+        CAIL_DBG("algorithm=%s (one rank)", cail_algo_name(CAIL_ALGO_COPY));
+        count_algo(CAIL_ALGO_COPY, msg);
+        const void *src = sendbuf == MPI_IN_PLACE ? recvbuf : sendbuf;
+        return cail_gpu_single_rank(src, recvbuf, msg) == 0 ? MPI_SUCCESS : MPI_ERR_OTHER;
+    }
+#endif
 
     // ---- NVLink device path
 #ifndef CAIL_HOST_PATH

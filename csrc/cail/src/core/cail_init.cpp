@@ -268,10 +268,11 @@ void cail_finalize(void) {
         const cail_stats_t &c = cail_counters;
         fprintf(stderr,
                 "[cail] stats: calls=%llu passthrough=%llu rd=%llu ring=%llu rab=%llu "
-                "one_shot=%llu two_shot=%llu nvls=%llu ce_two_shot=%llu bytes=%llu reg_hits=%llu reg_misses=%llu "
-                "device_errors=%llu\n",
+                "one_shot=%llu two_shot=%llu nvls=%llu ce_two_shot=%llu copy=%llu bytes=%llu reg_hits=%llu "
+                "reg_misses=%llu device_errors=%llu\n",
                 c.calls, c.passthrough, c.by_algo[1], c.by_algo[2], c.by_algo[3], c.by_algo[4],
-                c.by_algo[5], c.by_algo[6], c.by_algo[7], c.bytes, c.reg_hits, c.reg_misses, c.device_errors);
+                c.by_algo[5], c.by_algo[6], c.by_algo[7], c.by_algo[8], c.bytes, c.reg_hits, c.reg_misses,
+                c.device_errors);
     }
     if (s.profile && cail_prof_calls) {
         const double n = (double)cail_prof_calls;

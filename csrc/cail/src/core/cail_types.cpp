@@ -105,7 +105,7 @@ const char *cail_op_name(cail_op_t op) {
 
 const char *cail_algo_name(int a) {
     static const char *names[] = {"recursive_doubling", "ring", "rabenseifner",
-                                  "one_shot", "two_shot", "nvls", "ce_two_shot"};
+                                  "one_shot", "two_shot", "nvls", "ce_two_shot", "copy"};
     if (a == CAIL_ALGO_AUTO) return "auto";
     return (a >= 0 && a < CAIL_NUM_ALGOS) ? names[a] : "unknown";
 }

@@ -51,7 +51,8 @@ typedef enum {
     CAIL_ALGO_TWO_SHOT = 4,
     CAIL_ALGO_NVLS = 5,
     CAIL_ALGO_CE_TWO_SHOT = 6,
-    CAIL_NUM_ALGOS = 7
+    CAIL_ALGO_COPY = 7,          /* one-rank communicator: dst = src, chosen automatically */
+    CAIL_NUM_ALGOS = 8
 } cail_algo_t;
 
 /* Storage classes the kernels are instantiated for. */

@@ -37,6 +37,7 @@
 #include <sys/un.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <atomic>
 #include <list>
 #include <string>
@@ -120,10 +121,13 @@ void load_driver() {
 }
 
 // ---------------------------------------------------------------- constants
-constexpr size_t kFlagBytes = 64 << 10;                 // arrival flags (16 KiB used)
+constexpr size_t kFlagBytes = 64 << 10;                 // flags: one-shot, push RS, push AG (48 KiB used)
+static_assert(3 * cail::kFlagWords * sizeof(uint32_t) <= kFlagBytes, "flag arrays exceed the flag area");
 constexpr size_t kSlotBytes = 1 << 20;                  // one-shot: bytes per source slot
 constexpr size_t kScratchParity = kMaxRanks * kSlotBytes;  // one slot per source rank
-constexpr size_t kWorkspaceBytes = kFlagBytes + 2 * kScratchParity;
+constexpr size_t kPushOff = kFlagBytes + 2 * kScratchParity;  // push two-shot: RS area, then AG area
+constexpr size_t kDefaultPieceMax = 32 << 10;           // push two-shot: bytes per CTA, round and slice
+constexpr size_t kDefaultPieceMin = 4 << 10;
 constexpr size_t kNvlsCounterBytes = 2 << 20;           // counter page(s) of the multicast region
 constexpr size_t kDefaultNvlsSlot = 128ull << 20;       // NVLS: bytes per staging slot (3 slots)
 
@@ -216,6 +220,10 @@ struct cail_dev_comm {
     char *ws = nullptr;
     char *peer_ws[kMaxRanks] = {};
     uint32_t epoch = 0;
+    // push two-shot: CTAs per rank, largest piece, bytes per area, round epoch
+    int push_gmax = 0;
+    size_t push_piece_max = 0, push_area = 0;
+    uint32_t push_epoch = 0;
     DevStatus *status_h = nullptr, *status_d = nullptr;
     // host exchange
     XSlot *xs = nullptr;
@@ -622,10 +630,15 @@ void destroy_context(cail_dev_comm *dc) {
         for (int q = 0; q < dc->P; ++q)
             if (q != dc->rank && dc->peer_ws[q]) cudaIpcCloseMemHandle(dc->peer_ws[q]);
         if (dc->ws) cudaFree(dc->ws);
-        if (dc->status_h) cudaFreeHost(dc->status_h);
+        // the last stream-ordered call's status is read before the pinned
+        // block that holds it is released (the stream was synchronised above)
         if (dc->pending && dc->status_h && dc->status_h->code != 0)
             CAIL_ERR("a stream-ordered MPI_Allreduce on this communicator failed: rank %d gave up "
                      "waiting (block %d, epoch %u)", dc->status_h->rank, dc->status_h->block, dc->status_h->epoch);
+        dc->pending = false;
+        if (dc->status_h) cudaFreeHost(dc->status_h);
+        dc->status_h = nullptr;
+        dc->status_d = nullptr;
         if (dc->stream) cudaStreamDestroy(dc->stream);
         if (dc->legacy_ev) cudaEventDestroy(dc->legacy_ev);
         if (dc->done_ev) cudaEventDestroy(dc->done_ev);
@@ -633,6 +646,25 @@ void destroy_context(cail_dev_comm *dc) {
         if (prev >= 0) cudaSetDevice(prev);
     }
     delete dc;
+}
+
+// CAIL_TWOSHOT_PIECE_MAX / CAIL_TWOSHOT_PIECE_MIN (bytes, multiples of 16):
+// the largest and smallest piece a CTA of the push two-shot moves per round
+// and slice.  The largest one sizes the workspace (2 x 2 x G x P x piece).
+size_t env_bytes(const char *name, size_t dflt, size_t lo, size_t hi) {
+    const char *e = getenv(name);
+    if (!e || !*e) return dflt;
+    size_t v = (size_t)strtoull(e, nullptr, 10);
+    v = v / 16 * 16;
+    return v < lo ? lo : (v > hi ? hi : v);
+}
+size_t push_piece_max_env() {
+    static const size_t v = env_bytes("CAIL_TWOSHOT_PIECE_MAX", kDefaultPieceMax, 1024, (size_t)1 << 20);
+    return v;
+}
+size_t push_piece_min_env() {
+    static const size_t v = env_bytes("CAIL_TWOSHOT_PIECE_MIN", kDefaultPieceMin, 256, (size_t)1 << 20);
+    return v;
 }
 
 cail_dev_comm *create_context(MPI_Comm comm) {
@@ -686,7 +718,11 @@ cail_dev_comm *create_context(MPI_Comm comm) {
     ok = cudaStreamCreateWithFlags(&dc->stream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&dc->legacy_ev, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&dc->done_ev, cudaEventDisableTiming) == cudaSuccess;
-    ok = ok && cudaMalloc(&dc->ws, kWorkspaceBytes) == cudaSuccess;
+    // push two-shot areas: 2 parities x G CTAs x P sources x the largest piece
+    dc->push_gmax = cail::push_max_ctas(1, dc->sms);
+    dc->push_piece_max = push_piece_max_env();
+    dc->push_area = ((size_t)2 * dc->push_gmax * dc->P * dc->push_piece_max + 255) / 256 * 256;
+    ok = ok && cudaMalloc(&dc->ws, kPushOff + 2 * dc->push_area) == cudaSuccess;
     ok = ok && cudaMemset(dc->ws, 0, kFlagBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
     ok = ok && cudaHostAlloc((void **)&dc->status_h, sizeof(DevStatus), cudaHostAllocMapped) == cudaSuccess;
     ok = ok && cudaHostGetDevicePointer((void **)&dc->status_d, dc->status_h, 0) == cudaSuccess;
@@ -857,7 +893,68 @@ int run_oneshot_chunked(cail_dev_comm *dc, const char *src, char *dst, size_t co
     return check_status(dc, "one_shot");
 }
 
-// ---- two-shot over registered user buffers
+// ---- push two-shot over the IPC workspace (no host exchange)
+// Fills the slice table and the launch shape of a push two-shot of `count`
+// elements: slices cut at 16-byte units when every buffer is 16-byte
+// aligned (the last slice takes the ragged tail), else at elements; pieces
+// of at least CAIL_TWOSHOT_PIECE_MIN bytes so that small messages use few
+// CTAs, at most the workspace's piece; G CTAs; rounds to cover the longest
+// slice.  The same on every rank.
+void push_shape(cail::PushArgs &a, int P, size_t count, size_t esz, bool vec, int gmax, size_t piece_max,
+                size_t piece_min) {
+    const size_t bytes = count * esz;
+    const size_t unit = vec ? 16 : esz;
+    const size_t nunits = bytes / unit;
+    for (int q = 0; q < P; ++q) a.slice_off[q] = nunits * q / P * unit;
+    a.slice_off[P] = bytes;
+    size_t mx = 0;
+    for (int q = 0; q < P; ++q) mx = std::max(mx, a.slice_off[q + 1] - a.slice_off[q]);
+    a.max_slice = mx;
+    size_t piece = (mx + gmax - 1) / gmax;
+    piece = (piece + 15) / 16 * 16;
+    piece = std::min(std::max(piece, piece_min), piece_max);
+    a.piece = piece;
+    size_t g = (mx + piece - 1) / piece;
+    a.G = (int)std::max<size_t>(1, std::min<size_t>(g, (size_t)gmax));
+    a.rounds = (int)((mx + (size_t)a.G * piece - 1) / ((size_t)a.G * piece));
+    if (a.rounds < 1) a.rounds = 1;
+    a.P = P;
+    a.vec = vec ? 1 : 0;
+}
+
+int run_push(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec,
+             bool allow_ordered) {
+    cail::PushArgs a;
+    memset(&a, 0, sizeof(a));
+    const bool vec = (((uintptr_t)src | (uintptr_t)dst) & 15) == 0;
+    push_shape(a, dc->P, count, esz, vec, dc->push_gmax, dc->push_piece_max, push_piece_min_env());
+    a.rank0 = dc->rank;
+    a.src[dc->rank] = src;
+    a.dst[dc->rank] = dst;
+    for (int q = 0; q < dc->P; ++q) {
+        a.rs[q] = dc->peer_ws[q] + kPushOff;
+        a.ag[q] = dc->peer_ws[q] + kPushOff + dc->push_area;
+        a.flags[q] = (uint32_t *)dc->peer_ws[q];
+    }
+    a.epoch0 = dc->push_epoch + 1;
+    dc->push_epoch += (uint32_t)a.rounds;
+    a.timeout_ns = timeout_ns();
+    a.status = dc->status_d;
+    double t = cail_global_state.profile ? cail_now_us() : 0.0;
+    cudaError_t e = cail::launch_push(op, ec, a, 1, false, dc->stream);
+    cail_prof_mark(CAIL_PH_LAUNCH, t);
+    cail_counters.launches++;
+    if (e != cudaSuccess) {
+        CAIL_ERR("two_shot launch failed: %s", cudaGetErrorString(e));
+        dc->broken = true;
+        return MPI_ERR_OTHER;
+    }
+    if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc);
+    return check_status(dc, "two_shot");
+}
+
+// ---- two-shot over registered user buffers (zero-copy; host exchange of
+// the buffers' IPC handles and host barriers around the kernel)
 // ---- copy-engine two-shot
 // Rank r owns slice r of the message (cut at 16-byte units).  For each chunk
 // of its slice the copy engine pulls the P-1 peers' parts into local scratch
@@ -1182,6 +1279,16 @@ int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
     return check_status(dc, "nvls");
 }
 
+// CAIL_TWOSHOT_ZEROCOPY=1: two_shot runs the zero-copy kernel over the user
+// buffers (host exchange and barriers) instead of the push kernel.
+bool twoshot_zero_copy() {
+    static const bool v = [] {
+        const char *e = getenv("CAIL_TWOSHOT_ZEROCOPY");
+        return e && *e && *e != '0';
+    }();
+    return v;
+}
+
 // Built-in one_shot / two_shot crossover (measured on B200 at 2 to 8 ranks:
 // one_shot is ahead up to 512 KiB).  CAIL_TUNE_FILE lines replace it per
 // rank count.
@@ -1334,8 +1441,10 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
         rc = run_nvls(dc, src, dst, (size_t)count, esz, (int)op, ec);
     } else if (algo == CAIL_ALGO_CE_TWO_SHOT) {
         rc = run_twoshot(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
-    } else {
+    } else if (twoshot_zero_copy()) {
         rc = run_twoshot(dc, src, dst, (size_t)count, esz, (int)op, ec);
+    } else {
+        rc = run_push(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
     }
     if (prev >= 0 && prev != dc->dev) cudaSetDevice(prev);
     return rc;

@@ -55,6 +55,46 @@ struct TwoShotArgs {
     int unroll2;                     // process two vectors per loop iteration
 };
 
+// Push two-shot over the communicator's IPC workspace (no host exchange).
+// The message is cut into P slices (16-byte units; slice P-1 also holds the
+// ragged tail); slice q is reduced by rank q.  CTA b of every rank handles,
+// in round k, the piece of every slice at slice-relative byte offset
+// (k * G + b) * piece:
+//   1. it pushes its piece of slice q into RS slot (parity, b, rank) of rank
+//      q's workspace, for every q != rank (NVLink stores), and raises
+//      flag RS[rank][b] = epoch on each peer with st.release.sys;
+//   2. it waits for RS[q][b] >= epoch from every peer (ld.acquire.sys), folds
+//      the P pieces of its own slice in rank order (its own piece straight
+//      from the input), stores the result into its output and into AG slot
+//      (parity, b, rank) of every peer, and raises AG[rank][b];
+//   3. it waits for every peer's AG[q][b] and copies the gathered pieces of
+//      the other slices from its AG slots into its output.
+// Epochs grow by one per round, so flags never need resetting, and slots
+// alternate between two parities: round k + 2 of a CTA starts only after it
+// has received the peers' AG pieces of round k + 1, which each peer sends
+// after it finished reading its slots of round k.  No rank reads or writes
+// another rank's user buffers, so the call needs no host barrier and the
+// buffers are free for reuse as soon as the kernel has finished.
+// A launch may run several ranks' CTAs (the one-GPU emulation used by the
+// tests): CTA i belongs to rank rank0 + i / G and is CTA i % G of that rank.
+constexpr int kRsFlagBase = kFlagWords;      // word offsets in the flag array
+constexpr int kAgFlagBase = 2 * kFlagWords;
+struct PushArgs {
+    const char *src[kMaxRanks];      // input of each rank this launch runs (production: [rank])
+    char *dst[kMaxRanks];            // output of each rank this launch runs
+    char *rs[kMaxRanks];             // RS area of every rank's workspace (peer mappings)
+    char *ag[kMaxRanks];             // AG area of every rank's workspace (peer mappings)
+    uint32_t *flags[kMaxRanks];      // flag array of every rank (peer mappings)
+    size_t slice_off[kMaxRanks + 1]; // byte offset of slice q; slice_off[P] = message bytes
+    size_t max_slice;                // bytes of the longest slice
+    size_t piece;                    // bytes per CTA, round and slice (a multiple of 16)
+    int P, rank0, G, rounds;
+    uint32_t epoch0;                 // epoch of round 0
+    int vec;                         // every user buffer is 16-byte aligned
+    unsigned long long timeout_ns;
+    DevStatus *status;
+};
+
 // Pipelined NVLS allreduce of a whole message.  The message is cut into
 // sub-chunks that flow through a ring of 3 staging slots in a
 // multicast-bound region.  Iteration k (k = 0 .. K+1) copies sub-chunk k into
@@ -105,13 +145,23 @@ cudaError_t launch_twoshot(int op, int ec, const TwoShotArgs &a, int blocks, int
                            cudaStream_t s);
 cudaError_t launch_nvls(int op, int ec, const NvlsArgs &a, int blocks, int threads, cudaStream_t s);
 cudaError_t launch_fold(int op, int ec, const FoldArgs &a, int blocks, int threads, cudaStream_t s);
-// Device copy through TMA bulk copies (experimental, single-GPU harness only);
-// src and dst must share their alignment modulo 16.  *status gets 1 when a
-// wait ran out after spin_limit polls.
-cudaError_t launch_bulk_copy(char *dst, const char *src, size_t bytes, int blocks, unsigned long long spin_limit,
+// Push two-shot: a.G * ranks CTAs of 512 threads, where ranks = 1 in
+// production; cooperative = true launches it as a cooperative kernel (the
+// emulation of several ranks on one GPU, whose CTAs wait on one another).
+cudaError_t launch_push(int op, int ec, const PushArgs &a, int ranks, bool cooperative, cudaStream_t s);
+// Largest G for which `ranks` x G CTAs of the push kernel are co-resident.
+int push_max_ctas(int ranks, int sm_count);
+// Device copy through TMA bulk copies, one CTA per SM (large one-rank
+// copies); src and dst must share their alignment modulo 16.  *status gets 1
+// when a wait ran out after timeout_ns, 2 when the drain after it also did.
+cudaError_t launch_bulk_copy(char *dst, const char *src, size_t bytes, int sm_count, unsigned long long timeout_ns,
                              int *status, cudaStream_t s);
 // 1 if the NVLS kernel exists for (op, ec).
 int nvls_supported(int op, int ec);
+// Device-to-device copy of `bytes` bytes (the one-rank allreduce); src and dst
+// must share their alignment modulo 16.  16-byte vectors, eight loads in
+// flight per thread, at most two 512-thread CTAs per SM.
+cudaError_t launch_copy(char *dst, const char *src, size_t bytes, int sm_count, cudaStream_t s);
 // Element-wise local reduction io = op(io, in) (PMPI algorithm path).
 cudaError_t launch_reduce_local(int op, int ec, const void *in, void *io, size_t n, int sm_count,
                                 cudaStream_t s);

@@ -33,6 +33,12 @@ int cail_gpu_memcpy(void *dst, const void *src, size_t size);
 
 int cail_gpu_synchronize(void);
 
+/* The allreduce of a one-rank communicator: dst = src (nothing to do when they
+ * are the same buffer).  Runs on the legacy stream (stream sync mode 1) with
+ * cail's copy kernel, or cudaMemcpyAsync above CAIL_COPY_KERNEL_MAX bytes, and
+ * returns after completion unless stream-ordered completion is on.  0 or -1. */
+int cail_gpu_single_rank(const void *src, void *dst, size_t bytes);
+
 /* Read fence after a network receive into device memory: a 1-byte
  * device->host read of the last byte drains earlier posted writes (NIC RDMA,
  * GDRCopy stores).  No-op when CAIL_FLUSH_RECV=0 or in the host build. */

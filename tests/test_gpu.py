@@ -74,12 +74,16 @@ def test_native_library_loaded_in_process():
     assert os.path.join(LIB, "libcail.so") in r.stdout
 
 
-@pytest.mark.parametrize("algo", ["one_shot", "two_shot", "ce_two_shot"])
-def test_single_rank_kernels_all_types(algo):
+@pytest.mark.parametrize("copy_max", ["0", "134217728"], ids=["bulk_copy", "copy_kernel"])
+def test_single_rank_copy_all_types(copy_max):
+    """One rank: the allreduce is dst = src (a copy kernel below
+    CAIL_COPY_KERNEL_MAX, the TMA bulk copy above); every type and op,
+    separate and in place, against PMPI bit for bit."""
     need_gpus(1)
     r = mpirun(1, ["cail_check", "-m", "matrix", "-c", "100003", "-d", "-p", "--bits"], preload="cuda",
-               env={"CAIL_ALGO": algo, "CAIL_MIN_MSG_SIZE": "0"})
+               env={"CAIL_MIN_MSG_SIZE": "0", "CAIL_COPY_KERNEL_MAX": copy_max, "CAIL_STATS": "1"})
     assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+    assert "copy=" in r.stderr and " copy=0 " not in r.stderr
 
 
 @pytest.mark.parametrize("algo", ["recursive_doubling", "ring", "rabenseifner", "auto"])
