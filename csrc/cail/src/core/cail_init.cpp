@@ -31,7 +31,7 @@ cail_state_t cail_global_state = {
     /*force_algo*/ CAIL_ALGO_AUTO,
     /*device_timeout_ms*/ CAIL_DEFAULT_DEVICE_TIMEOUT_MS,
     /*nvls*/ 1, /*oneshot_max*/ 0, /*flush_recv*/ 1, /*stats*/ 0, /*trace*/ nullptr,
-    /*stream_sync*/ 1, /*profile*/ 0, /*stream_ordered*/ 0, /*nvtx*/ 0};
+    /*stream_sync*/ 1, /*profile*/ 0, /*stream_ordered*/ 0, /*nvtx*/ 0, /*device_checks*/ 0};
 
 cail_stats_t cail_counters;
 int cail_last_algo = -2;  // -2: none yet, -3: passthrough
@@ -234,6 +234,7 @@ void cail_load_config(void) {
     }
     if ((e = env_nonempty(CAIL_ENV_TUNE_FILE))) load_tune(e);
     if ((e = env_nonempty("CAIL_NVTX"))) s.nvtx = e[0] != '0';
+    if ((e = env_nonempty(CAIL_ENV_DEVICE_CHECKS))) s.device_checks = e[0] != '0';
 }
 
 const cail_tune_t *cail_tune_for(int nranks) {

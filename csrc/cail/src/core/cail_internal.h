@@ -38,6 +38,7 @@
 #define CAIL_ENV_FLUSH_RECV "CAIL_FLUSH_RECV"
 #define CAIL_ENV_STREAM_SYNC "CAIL_STREAM_SYNC"
 #define CAIL_ENV_STREAM_ORDERED "CAIL_STREAM_ORDERED"
+#define CAIL_ENV_DEVICE_CHECKS "CAIL_DEVICE_CHECKS"
 
 #define CAIL_DEFAULT_MSG_SMALL_THRESHOLD 262144U /* 256 KiB */
 #define CAIL_DEFAULT_NPROCS_THRESHOLD 4U
@@ -71,6 +72,7 @@ typedef struct cail_state {
     int profile;                 /* CAIL_PROFILE: host-side phase timers */
     int stream_ordered;          /* one-shot calls complete in stream order, not on the host */
     int nvtx;                    /* CAIL_NVTX: an NVTX range per call (CUDA build) */
+    int device_checks;           /* CAIL_DEVICE_CHECKS: kernels validate their arguments and bounds */
 } cail_state_t;
 
 /* Opt-in host-side phase timers (CAIL_PROFILE=1), averaged per call and

@@ -128,8 +128,10 @@ constexpr size_t kScratchParity = kMaxRanks * kSlotBytes;  // one slot per sourc
 constexpr size_t kPushOff = kFlagBytes + 2 * kScratchParity;  // push two-shot: RS area, then AG area
 constexpr size_t kDefaultPieceMax = 32 << 10;           // push two-shot: bytes per CTA, round and slice
 constexpr size_t kDefaultPieceMin = 4 << 10;
-constexpr size_t kNvlsCounterBytes = 2 << 20;           // counter page(s) of the multicast region
-constexpr size_t kDefaultNvlsSlot = 128ull << 20;       // NVLS: bytes per staging slot (3 slots)
+constexpr size_t kNvlsStepsOff = 3 * cail::kFlagWords * sizeof(uint32_t);  // NVLS per-CTA steps, in the flag area
+static_assert(kNvlsStepsOff + cail::kMaxBlocks * sizeof(uint32_t) <= kFlagBytes, "flag area too small");
+constexpr size_t kNvlsCtrRegion = (cail::kNvlsCtrBytes + 65535) / 65536 * 65536;  // counters, then staging
+constexpr size_t kDefaultNvlsUnit = 256 << 10;          // NVLS: largest bytes per CTA and step
 
 // ---------------------------------------------------------------- host exchange
 struct BufDesc {
@@ -236,12 +238,10 @@ struct cail_dev_comm {
     std::list<ImportKey> lru;
     // NVLS
     bool nvls = false;
-    size_t nvls_slot = 0, nvls_size = 0;
+    size_t nvls_unit = 0, nvls_size = 0;
     CUmemGenericAllocationHandle mc_handle = 0, phys_handle = 0;
     CUdeviceptr uc_va = 0, mc_va = 0;
     bool mc_bound = false;
-    uint32_t nvls_expected = 0;        // multicast counter value after the last call
-    uint32_t nvls_local_expected = 0;  // local arrival counter value after the last call
     int nvls_blocks = 0;
     double last_live_check = 0.0;
     cudaEvent_t legacy_ev = nullptr;  // marks the legacy stream's queue at call entry
@@ -288,14 +288,42 @@ int find_ordinal(const char uuid[16]) {
 }
 
 // ---- host barrier over the exchange segment
+// Waits until every rank's arrive (depart) word reaches seq.  Bounded: a peer
+// that has exited fails the wait at once, and a live peer that does not
+// arrive within CAIL_HOST_TIMEOUT_MS (default: the device timeout) fails it
+// at the deadline.  On failure this rank's own word is switched to
+// seq | kXErr (unless it already moved on), so that a peer arriving late
+// sees the failure instead of starting the collective, and
+// MPI_ERR_OTHER is returned; the caller marks the communicator broken.
+long host_timeout_ms() {
+    static const long v = [] {
+        const char *e = getenv("CAIL_HOST_TIMEOUT_MS");
+        long t = e && *e ? atol(e) : 0;
+        return t > 0 ? t : 0;
+    }();
+    return v > 0 ? v : cail_global_state.device_timeout_ms;
+}
+
 int host_wait(cail_dev_comm *dc, bool depart, uint64_t seq) {
     unsigned spins = 0;
+    const double deadline = cail_now_us() + 1000.0 * (double)host_timeout_ms();
+    std::atomic<uint64_t> &mine = depart ? dc->xs[dc->rank].depart : dc->xs[dc->rank].arrive;
     for (int q = 0; q < dc->P; ++q) {
+        // a peer that gave up at this call's arrive barrier never departs
+        if (depart && dc->xs[q].arrive.load(std::memory_order_acquire) == (seq | kXErr)) continue;
         std::atomic<uint64_t> &a = depart ? dc->xs[q].depart : dc->xs[q].arrive;
-        while (a.load(std::memory_order_acquire) < seq) {
-            if (++spins % 65536 == 0) {
-                if (process_gone(dc->peer_pid[q])) {
-                    CAIL_ERR("rank %d: peer rank %d (pid %d) is gone", dc->rank, q, dc->peer_pid[q]);
+        while ((a.load(std::memory_order_acquire) & ~kXErr) < seq) {
+            if (++spins % 4096 == 0) {
+                const bool gone = process_gone(dc->peer_pid[q]);
+                if (gone || cail_now_us() > deadline) {
+                    if (gone)
+                        CAIL_ERR("rank %d: peer rank %d (pid %d) is gone", dc->rank, q, dc->peer_pid[q]);
+                    else
+                        CAIL_ERR("rank %d: peer rank %d did not reach the %s barrier of call %llu within %ld ms "
+                                 "(CAIL_HOST_TIMEOUT_MS)",
+                                 dc->rank, q, depart ? "depart" : "arrive", (unsigned long long)seq, host_timeout_ms());
+                    uint64_t cur = seq;
+                    mine.compare_exchange_strong(cur, seq | kXErr, std::memory_order_acq_rel);
                     return MPI_ERR_OTHER;
                 }
                 if (spins > (1u << 20)) sched_yield();
@@ -514,11 +542,13 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
         CAIL_DBG("nvls: driver entry points missing");
         return;
     }
-    size_t slot = kDefaultNvlsSlot;
-    if (const char *e = getenv("CAIL_NVLS_CHUNK")) {
+    // CAIL_NVLS_UNIT: largest bytes per CTA and step (a multiple of 64 KiB)
+    size_t unit = kDefaultNvlsUnit;
+    if (const char *e = getenv("CAIL_NVLS_UNIT")) {
         long v = atol(e);
-        if (v >= (1 << 20)) slot = ((size_t)v + 65535) / 65536 * 65536;
+        if (v >= (64 << 10) && v <= (64 << 20)) unit = (size_t)v / 65536 * 65536;
     }
+    const int blocks = cail::nvls_max_ctas(dc->sms);
     CUdevice cd = 0;
     bool ok = nvls_step(dc, true, g_drv.deviceGet(&cd, dc->dev), "cuDeviceGet");
     CUmulticastObjectProp mp;
@@ -532,17 +562,18 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     ap.location.id = cd;
     ap.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;  // as the multicast object
     size_t g1 = 0, g2 = 0;
-    mp.size = kNvlsCounterBytes + cail::kNvlsSlots * slot;
-    ok = nvls_step(dc, ok, g_drv.multicastGetGranularity(&g1, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED),
+    const size_t want = kNvlsCtrRegion + (size_t)blocks * unit;
+    mp.size = want;
+    ok = nvls_step(dc, ok, g_drv.multicastGetGranularity(&g1, &mp, CU_MULTICAST_GRANULARITY_MINIMUM),
                    "cuMulticastGetGranularity");
-    ok = nvls_step(dc, ok, g_drv.memGetAllocationGranularity(&g2, &ap, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED),
+    ok = nvls_step(dc, ok, g_drv.memGetAllocationGranularity(&g2, &ap, CU_MEM_ALLOC_GRANULARITY_MINIMUM),
                    "cuMemGetAllocationGranularity");
     size_t gran = g1 > g2 ? g1 : g2;
     if (gran == 0) gran = 2 << 20;
-    size_t size = (kNvlsCounterBytes + cail::kNvlsSlots * slot + gran - 1) / gran * gran;
+    size_t size = (want + gran - 1) / gran * gran;
     mp.size = size;
     dc->nvls_size = size;
-    dc->nvls_slot = slot;
+    dc->nvls_unit = unit;
     if (!agree(dc->comm, ok)) return;
 
     int fd = -1;
@@ -587,17 +618,16 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     ok = nvls_step(dc, ok, g_drv.memAddressReserve(&dc->mc_va, size, gran, 0, 0), "cuMemAddressReserve(mc)");
     ok = nvls_step(dc, ok, g_drv.memMap(dc->mc_va, size, 0, dc->mc_handle, 0), "cuMemMap(mc)");
     ok = nvls_step(dc, ok, g_drv.memSetAccess(dc->mc_va, size, &acc, 1), "cuMemSetAccess(mc)");
-    if (ok && (cudaMemset((void *)dc->uc_va, 0, kNvlsCounterBytes) != cudaSuccess ||
+    if (ok && (cudaMemset((void *)dc->uc_va, 0, kNvlsCtrRegion) != cudaSuccess ||
                cudaDeviceSynchronize() != cudaSuccess)) {
         CAIL_DBG("nvls: rank %d: clearing the counters failed", dc->rank);
         ok = false;
     }
     if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }
-    // two 512-thread CTAs per SM are always co-resident, which the
-    // grid-wide counter barrier of the NVLS kernel requires
-    dc->nvls_blocks = dc->sms * 2;
+    dc->nvls_blocks = blocks;
     dc->nvls = true;
-    CAIL_DBG("nvls: multicast region of %zu bytes (granularity %zu), staging %d x %zu", size, gran, cail::kNvlsSlots, slot);
+    CAIL_DBG("nvls: multicast region of %zu bytes (granularity %zu), %d CTA slots of %zu bytes", size, gran, blocks,
+             unit);
 }
 
 void ce_teardown(cail_dev_comm *dc) {
@@ -791,10 +821,14 @@ int check_status(cail_dev_comm *dc, const char *what) {
     }
     if (dc->status_h->code != 0) {
         const DevStatus &s = *dc->status_h;
-        CAIL_ERR("%s: rank %d gave up after %ld ms waiting for %s %d (block %d, epoch %u, saw %u)",
-                 what, s.rank, cail_global_state.device_timeout_ms,
-                 s.waited_on >= 0 ? "rank" : "barrier", s.waited_on >= 0 ? s.waited_on : -1 - s.waited_on,
-                 s.block, s.epoch, s.seen);
+        if (s.code == 2)
+            CAIL_ERR("%s: rank %d: device argument check %d failed (CAIL_DEVICE_CHECKS); the kernel did not run",
+                     what, s.rank, s.waited_on);
+        else
+            CAIL_ERR("%s: rank %d gave up after %ld ms waiting for %s %d (block %d, epoch %u, saw %u)",
+                     what, s.rank, cail_global_state.device_timeout_ms,
+                     s.waited_on >= 0 ? "rank" : "barrier", s.waited_on >= 0 ? s.waited_on : -1 - s.waited_on,
+                     s.block, s.epoch, s.seen);
         memset(dc->status_h, 0, sizeof(DevStatus));
         dc->broken = true;
         return MPI_ERR_OTHER;
@@ -826,6 +860,7 @@ int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     a.my_flags = (uint32_t *)dc->ws;
     a.timeout_ns = timeout_ns();
     a.status = dc->status_d;
+    a.checks = cail_global_state.device_checks;
     // ~2 vectors per thread, 512 threads per block
     size_t vec = (bytes + 15) / 16;
     int threads = 512;
@@ -940,6 +975,8 @@ int run_push(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
     dc->push_epoch += (uint32_t)a.rounds;
     a.timeout_ns = timeout_ns();
     a.status = dc->status_d;
+    a.area = dc->push_area;
+    a.checks = cail_global_state.device_checks;
     double t = cail_global_state.profile ? cail_now_us() : 0.0;
     cudaError_t e = cail::launch_push(op, ec, a, 1, false, dc->stream);
     cail_prof_mark(CAIL_PH_LAUNCH, t);
@@ -1118,7 +1155,10 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     double th = cail_global_state.profile ? cail_now_us() : 0.0;
     int rc = host_wait(dc, false, seq);
     th = cail_prof_mark(CAIL_PH_HOSTSYNC, th);
-    if (rc != MPI_SUCCESS) return rc;
+    if (rc != MPI_SUCCESS) {
+        dc->broken = true;
+        return rc;
+    }
     bool all_ok = true;
     for (int q = 0; q < dc->P; ++q) all_ok = all_ok && dc->xs[q].send.ok && dc->xs[q].recv.ok;
     if (!pre_ok || peer_failed(dc, false)) {
@@ -1223,52 +1263,37 @@ depart:
 }
 
 // ---- NVLS
-int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec) {
-    const int blocks = dc->nvls_blocks;
-    static const int copy_pct = [] {
-        const char *e = getenv("CAIL_NVLS_COPY_PCT");
-        int v = e ? atoi(e) : 50;
-        return v >= 10 && v <= 90 ? v : 50;
-    }();
-    // Sub-chunk: an eighth of the message (every pipeline stage costs one
-    // cross-GPU barrier, 6.4 us measured at 8 GPUs, and one fill/drain step,
-    // so stages stay few while copies still overlap), between 4 MiB and one
-    // staging slot, in 64 KiB units.  CAIL_NVLS_STAGES overrides the eighth;
-    // 4, 8 and 16 stages measured the same at 1 GiB (3.14-3.16 ms, 8 GPUs).
-    static const size_t stages = [] {
-        const char *e = getenv("CAIL_NVLS_STAGES");
-        long v = e ? atol(e) : 8;
-        return (size_t)(v >= 1 && v <= 1024 ? v : 8);
-    }();
-    size_t sub_bytes = count * esz / stages;
-    sub_bytes = sub_bytes < ((size_t)4 << 20) ? ((size_t)4 << 20) : sub_bytes;
-    sub_bytes = (sub_bytes + 65535) / 65536 * 65536;
-    if (sub_bytes > dc->nvls_slot) sub_bytes = dc->nvls_slot;
+// One launch; every CTA runs its own pipeline over units of at most
+// CAIL_NVLS_UNIT bytes (see NvlsArgs).  The unit shrinks for small messages
+// so that every CTA has work, in 64 KiB steps down to 16 KiB.
+int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec,
+             bool allow_ordered) {
+    const size_t bytes = count * esz;
+    const int G = dc->nvls_blocks;
+    size_t unit = (bytes + G - 1) / G;
+    unit = unit <= (16 << 10) ? (16 << 10) : (unit + 65535) / 65536 * 65536;
+    if (unit > dc->nvls_unit) unit = dc->nvls_unit;
+    const size_t units = (bytes + unit - 1) / unit;
+    const int blocks = (int)(units < (size_t)G ? units : (size_t)G);
     cail::NvlsArgs a;
     memset(&a, 0, sizeof(a));
     a.src = src;
     a.dst = dst;
-    a.uc = (char *)dc->uc_va + kNvlsCounterBytes;
-    a.mc = (char *)dc->mc_va + kNvlsCounterBytes;
-    a.mc_counter = (uint32_t *)dc->mc_va;
-    a.uc_counter = (const uint32_t *)dc->uc_va;
-    a.local_counter = (uint32_t *)((char *)dc->uc_va + 256);  // never written through the multicast view
-    a.count = count;
-    a.sub = sub_bytes / esz;
-    a.slot_bytes = dc->nvls_slot;
+    a.uc = (char *)dc->uc_va + kNvlsCtrRegion;
+    a.mc = (char *)dc->mc_va + kNvlsCtrRegion;
+    a.mc_ctr = (char *)dc->mc_va;
+    a.uc_ctr = (const char *)dc->uc_va;
+    a.steps = (uint32_t *)(dc->ws + kNvlsStepsOff);
+    a.bytes = bytes;
+    a.unit = unit;
+    a.area = dc->nvls_size - kNvlsCtrRegion;
     a.P = dc->P;
     a.rank = dc->rank;
-    a.copy_blocks = blocks * copy_pct / 100;
-    a.target0 = dc->nvls_expected;
-    a.local0 = dc->nvls_local_expected;
     a.timeout_ns = timeout_ns();
     a.status = dc->status_d;
-    const size_t nsub = (count + a.sub - 1) / a.sub;
-    // one barrier per pipeline iteration: P cross-rank arrivals, `blocks` local ones
-    dc->nvls_expected += (uint32_t)(nsub + 2) * (uint32_t)dc->P;
-    dc->nvls_local_expected += (uint32_t)(nsub + 2) * (uint32_t)blocks;
+    a.checks = cail_global_state.device_checks;
     double t = cail_global_state.profile ? cail_now_us() : 0.0;
-    cudaError_t e = cail::launch_nvls(op, ec, a, blocks, 512, dc->stream);
+    cudaError_t e = cail::launch_nvls(op, ec, a, blocks, dc->stream);
     cail_prof_mark(CAIL_PH_LAUNCH, t);
     cail_counters.launches++;
     if (e != cudaSuccess) {
@@ -1276,6 +1301,7 @@ int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
         dc->broken = true;
         return MPI_ERR_OTHER;
     }
+    if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc);
     return check_status(dc, "nvls");
 }
 
@@ -1438,7 +1464,7 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
     if (algo == CAIL_ALGO_ONE_SHOT) {
         rc = run_oneshot_chunked(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
     } else if (algo == CAIL_ALGO_NVLS && cail_dev_nvls_ok(dc, dt, op)) {
-        rc = run_nvls(dc, src, dst, (size_t)count, esz, (int)op, ec);
+        rc = run_nvls(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
     } else if (algo == CAIL_ALGO_CE_TWO_SHOT) {
         rc = run_twoshot(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
     } else if (twoshot_zero_copy()) {

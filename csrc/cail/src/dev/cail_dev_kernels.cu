@@ -90,6 +90,19 @@ __device__ void report(DevStatus *st, int rank, int peer, int block, uint32_t ep
     }
 }
 
+// Argument check failure (CAIL_DEVICE_CHECKS): code 2, the check's number in
+// waited_on; reported once by CTA 0's thread 0.
+__device__ void report_check(DevStatus *st, int rank, int check) {
+    if (blockIdx.x == 0 && threadIdx.x == 0 && atomicCAS(&st->code, 0, 2) == 0) {
+        st->rank = rank;
+        st->waited_on = check;
+        st->block = 0;
+        st->epoch = 0;
+        st->seen = 0;
+        __threadfence_system();
+    }
+}
+
 // ---------------------------------------------------------------- one-shot
 // Pushes bytes [lo, hi) of src (any alignment) into P destinations (16-byte
 // aligned slots), 16 bytes at a time where src allows it.
@@ -114,9 +127,30 @@ __device__ __forceinline__ void block_push(char *const *dst, int P, const char *
     }
 }
 
+// CAIL_DEVICE_CHECKS for the one-shot kernel: 0 when the arguments are
+// consistent, else the number of the failed check.
+template <typename T>
+__device__ int oneshot_check(const OneShotArgs &a) {
+    if (a.P < 1 || a.P > kMaxRanks || a.rank < 0 || a.rank >= a.P) return 1;
+    if (gridDim.x > (unsigned)kMaxBlocks) return 2;
+    if (a.count > a.slot_bytes / sizeof(T)) return 3;
+    if (a.slot_bytes % 16 || ((uintptr_t)a.slot_in & 15)) return 4;
+    for (int q = 0; q < a.P; ++q)
+        if (!a.slot_out[q] || ((uintptr_t)a.slot_out[q] & 15) || !a.peer_flags[q]) return 5;
+    if (!a.src || !a.dst || !a.my_flags) return 6;
+    return 0;
+}
+
 template <int OP, typename T>
 __global__ void __launch_bounds__(512) oneshot_kernel(OneShotArgs a) {
     __shared__ int s_fail;
+    if (a.checks) {
+        const int bad = oneshot_check<T>(a);
+        if (bad) {
+            report_check(a.status, a.rank, bad);
+            return;
+        }
+    }
     const size_t bytes = a.count * sizeof(T);
     const size_t n16 = (bytes + 15) / 16;
     const size_t per = (n16 + gridDim.x - 1) / gridDim.x;
@@ -296,9 +330,46 @@ __device__ __forceinline__ void push_signal(const PushArgs &a, int me, int b, in
     if (t < a.P && t != me) st_release_sys(a.flags[t] + base + me * kMaxBlocks + b, e);
 }
 
+// CAIL_DEVICE_CHECKS for the push two-shot: 0 when the arguments are
+// consistent, else the number of the failed check.
+template <typename T>
+__device__ int push_check(const PushArgs &a) {
+    if (a.P < 2 || a.P > kMaxRanks) return 1;
+    if (a.G < 1 || a.G > kMaxBlocks || gridDim.x % (unsigned)a.G != 0 || a.rank0 < 0 ||
+        a.rank0 + (int)(gridDim.x / (unsigned)a.G) > a.P)
+        return 2;
+    if (a.piece == 0 || a.piece % 16) return 3;
+    if ((size_t)2 * a.G * a.P * a.piece > a.area) return 4;
+    size_t mx = 0;
+    if (a.slice_off[0] != 0) return 5;
+    for (int q = 0; q < a.P; ++q) {
+        if (a.slice_off[q + 1] < a.slice_off[q] || a.slice_off[q] % sizeof(T)) return 5;
+        if (a.vec && a.slice_off[q] % 16) return 5;
+        mx = max(mx, a.slice_off[q + 1] - a.slice_off[q]);
+    }
+    if (mx != a.max_slice || a.slice_off[a.P] % sizeof(T)) return 5;
+    if (a.rounds < 1 || (size_t)a.rounds * a.G * a.piece < a.max_slice) return 6;
+    for (int q = 0; q < a.P; ++q) {
+        if (!a.rs[q] || !a.ag[q] || !a.flags[q] || ((uintptr_t)a.rs[q] & 15) || ((uintptr_t)a.ag[q] & 15)) return 7;
+    }
+    for (int r = a.rank0; r < a.rank0 + (int)(gridDim.x / (unsigned)a.G); ++r) {
+        if (!a.src[r] || !a.dst[r]) return 8;
+        if (a.vec && ((((uintptr_t)a.src[r]) | ((uintptr_t)a.dst[r])) & 15)) return 8;
+        if (((uintptr_t)a.src[r] | (uintptr_t)a.dst[r]) % sizeof(T)) return 8;
+    }
+    return 0;
+}
+
 template <int OP, typename T, bool VEC>
 __global__ void __launch_bounds__(512, 2) push_kernel(PushArgs a) {
     __shared__ int s_fail;
+    if (a.checks) {
+        const int bad = push_check<T>(a);
+        if (bad) {
+            report_check(a.status, a.rank0, bad);
+            return;
+        }
+    }
     const int me = a.rank0 + (int)(blockIdx.x / (unsigned)a.G);
     const int b = (int)(blockIdx.x % (unsigned)a.G);
     const int P = a.P;
@@ -443,124 +514,122 @@ template <> struct Mm<CAIL_SUM, CAIL_EC_F32> {
 
 __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
-// Grid-wide + cross-rank barrier of pipeline iteration k, called by thread 0
-// of every CTA after a block barrier.  Two levels, so the multicast counter
-// takes one atomic per rank instead of one per CTA:
-//   1. fence, then arrive on this GPU's local counter; the CTA that arrives
-//      last (all gridDim.x arrivals of this iteration seen) fences again and
-//      adds 1 to the multicast counter on every GPU with one multimem.red;
-//   2. every CTA waits until its GPU's copy of the multicast counter shows
-//      the arrival of all P ranks.
-// The fence / atomic / fence chain orders every CTA's stores before the
-// release of the multimem.red.
-__device__ __forceinline__ bool nvls_barrier(const NvlsArgs &a, size_t k) {
-    __threadfence();
-    const uint32_t old = atomicAdd(a.local_counter, 1u);
-    if (old + 1u == a.local0 + (uint32_t)(k + 1) * gridDim.x) {
-        __threadfence();
-        fence_proxy_alias();
-        asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.mc_counter), "r"(1u)
-                     : "memory");
-    }
-    const uint32_t target = a.target0 + (uint32_t)(k + 1) * (uint32_t)a.P;
+// Cross-rank meeting of CTA b for one step, called by thread 0 after a block
+// barrier: a system-scope fence orders the CTA's earlier stores (made
+// visible to the block by the barrier) before the release of the
+// multimem.red that adds 1 to counter `ctr` on every GPU; then it polls this
+// GPU's copy of the counter until `target` arrivals.  false on timeout.
+__device__ __forceinline__ bool nvls_meet(const NvlsArgs &a, size_t ctr, uint32_t target, int b, int which) {
+    __threadfence_system();
+    fence_proxy_alias();
+    asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.mc_ctr + ctr), "r"(1u) : "memory");
     uint32_t seen = 0;
-    unsigned long long deadline = globaltimer() + a.timeout_ns;
-    if (!wait_flag(a.uc_counter, target, deadline, &seen)) {
-        report(a.status, a.rank, -1 - (int)k, blockIdx.x, target, seen);
+    const unsigned long long deadline = globaltimer() + a.timeout_ns;
+    if (!wait_flag(reinterpret_cast<const uint32_t *>(a.uc_ctr + ctr), target, deadline, &seen)) {
+        report(a.status, a.rank, -1 - which, b, target, seen);
         return false;
     }
     return true;
 }
 
-// Copies n bytes with the threads [part_tid, part_tid + part_threads) of the
-// grid; 16-byte vectors when both ends are aligned.
+// n bytes between this GPU's buffers with the CTA's threads; 16-byte
+// vectors (four in flight per thread) when both ends are aligned.
 template <typename T>
-__device__ __forceinline__ void part_copy(char *dst, const char *src, size_t n, size_t part_tid,
-                                          size_t part_threads) {
-    const size_t stride = part_threads;
-    const size_t tid = part_tid;
+__device__ __forceinline__ void cta_copy(char *dst, const char *src, size_t n) {
+    size_t done = 0;
     if ((((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
+        constexpr int U = 4;
         const size_t nv = n / 16;
-        for (size_t i = tid; i < nv; i += stride)
-            st_v4(dst + i * 16, *reinterpret_cast<const uint4 *>(src + i * 16));
-        for (size_t e = nv * 16 / sizeof(T) + tid; e < n / sizeof(T); e += stride)
-            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
-    } else {
-        for (size_t e = tid; e < n / sizeof(T); e += stride)
-            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+        size_t i = threadIdx.x;
+        for (; i + (U - 1) * blockDim.x < nv; i += U * blockDim.x) {
+            uint4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) v[u] = ld_v4(src + (i + u * blockDim.x) * 16);
+#pragma unroll
+            for (int u = 0; u < U; ++u) st_v4(dst + (i + u * blockDim.x) * 16, v[u]);
+        }
+        for (; i < nv; i += blockDim.x) st_v4(dst + i * 16, ld_v4(src + i * 16));
+        done = nv * 16;
     }
+    for (size_t e = done / sizeof(T) + threadIdx.x; e < n / sizeof(T); e += blockDim.x)
+        reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
 }
 
-template <typename T>
-__device__ __forceinline__ void grid_copy(char *dst, const char *src, size_t n) {
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if ((((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
-        const size_t nv = n / 16;
-        for (size_t i = tid; i < nv; i += stride)
-            st_v4(dst + i * 16, *reinterpret_cast<const uint4 *>(src + i * 16));
-        for (size_t e = nv * 16 / sizeof(T) + tid; e < n / sizeof(T); e += stride)
-            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
-    } else {
-        for (size_t e = tid; e < n / sizeof(T); e += stride)
-            reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
-    }
+// CAIL_DEVICE_CHECKS for the NVLS kernel: 0 when the arguments are
+// consistent, else the number of the failed check.
+template <typename T, int MB>
+__device__ int nvls_check(const NvlsArgs &a) {
+    if (a.P < 2 || a.P > kMaxRanks || a.rank < 0 || a.rank >= a.P) return 1;
+    if (gridDim.x > (unsigned)kMaxBlocks) return 2;
+    if (a.unit == 0 || a.unit % 16 || a.unit % MB) return 3;
+    if ((size_t)gridDim.x * a.unit > a.area) return 4;
+    if (((uintptr_t)a.uc | (uintptr_t)a.mc) & 15) return 5;
+    if (!a.src || !a.dst || !a.mc_ctr || !a.uc_ctr || !a.steps) return 6;
+    if (a.bytes % sizeof(T) || ((uintptr_t)a.src | (uintptr_t)a.dst) % sizeof(T)) return 7;
+    return 0;
 }
 
-// Two CTAs of 512 threads per SM must be co-resident (the barrier is grid
-// wide), hence the register cap of __launch_bounds__(512, 2).
 template <int OP, int EC>
 __global__ void __launch_bounds__(512, 2) nvls_kernel(NvlsArgs a) {
     using T = typename EcType<EC>::T;
     using M = Mm<OP, EC>;
     __shared__ int s_fail;
-    if (threadIdx.x == 0) s_fail = 0;
-    const size_t nsub = (a.count + a.sub - 1) / a.sub;
-    auto sub_elems = [&](size_t j) { return min(a.sub, a.count - j * a.sub); };
-    // Roles: the first copy_blocks CTAs move data between the user buffers
-    // and the staging slots (HBM), the others run the multimem reduction
-    // (NVLink), so both kinds of traffic are in flight at the same time.
-    const bool copier = (int)blockIdx.x < a.copy_blocks;
-    const size_t ctid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const size_t cthreads = (size_t)a.copy_blocks * blockDim.x;
-    const size_t rtid = (size_t)(blockIdx.x - a.copy_blocks) * blockDim.x + threadIdx.x;
-    const size_t rthreads = (size_t)(gridDim.x - a.copy_blocks) * blockDim.x;
-    constexpr int U = 4;  // multimem units in flight per thread
-
-    for (size_t k = 0; k < nsub + 2; ++k) {
-        if (copier) {
-            if (k < nsub)  // copy-in of sub-chunk k
-                part_copy<T>(a.uc + (k % kNvlsSlots) * a.slot_bytes, a.src + k * a.sub * sizeof(T),
-                             sub_elems(k) * sizeof(T), ctid, cthreads);
-            if (k >= 2) {  // copy-out of sub-chunk k-2
-                const size_t j = k - 2;
-                part_copy<T>(a.dst + j * a.sub * sizeof(T), a.uc + (j % kNvlsSlots) * a.slot_bytes,
-                             sub_elems(j) * sizeof(T), ctid, cthreads);
-            }
-        } else if (k >= 1 && k <= nsub) {  // reduce + broadcast this rank's slice of sub-chunk k-1
-            const size_t j = k - 1;
-            // the last unit may run past the data into the slot's padding;
-            // only real bytes are copied out
-            const size_t units = (sub_elems(j) * sizeof(T) + M::bytes - 1) / M::bytes;
-            const size_t lo = units * a.rank / a.P, hi = units * (a.rank + 1) / a.P;
-            char *mc = a.mc + (j % kNvlsSlots) * a.slot_bytes;
-            for (size_t u = lo + rtid; u < hi; u += U * rthreads) {
-                typename M::V v[U];
-#pragma unroll
-                for (int q = 0; q < U; ++q)
-                    if (u + q * rthreads < hi) v[q] = M::ld(mc + (u + q * rthreads) * M::bytes);
-#pragma unroll
-                for (int q = 0; q < U; ++q)
-                    if (u + q * rthreads < hi) M::st(mc + (u + q * rthreads) * M::bytes, v[q]);
-            }
+    if (a.checks) {
+        const int bad = nvls_check<T, M::bytes>(a);
+        if (bad) {
+            report_check(a.status, a.rank, bad);
+            return;
         }
-        fence_proxy_alias();
+    }
+    const int b = blockIdx.x;
+    const int G = gridDim.x;
+    if (threadIdx.x == 0) s_fail = 0;
+    const uint32_t base = a.steps[b];  // read before any thread of this CTA can update it
+    __syncthreads();
+    char *slot_uc = a.uc + (size_t)b * a.unit;
+    char *slot_mc = a.mc + (size_t)b * a.unit;
+    const size_t ctr_a = (size_t)b * kNvlsCtrStride;
+    const size_t ctr_b = ((size_t)kMaxBlocks + b) * kNvlsCtrStride;
+    constexpr int U = 4;  // multimem units in flight per thread
+    uint32_t k = 0;
+    for (;; ++k) {
+        const size_t off = ((size_t)k * G + b) * a.unit;
+        if (off >= a.bytes) break;  // the same on every rank
+        const size_t n = min(a.unit, a.bytes - off);
+        const uint32_t target = (base + k + 1) * (uint32_t)a.P;
+
+        // 1. copy-in, 2. meet on A
+        cta_copy<T>(slot_uc, a.src + off, n);
         __syncthreads();
-        if (threadIdx.x == 0 && !nvls_barrier(a, k)) s_fail = 1;
+        if (threadIdx.x == 0 && !nvls_meet(a, ctr_a, target, b, 0)) s_fail = 1;
         __syncthreads();
         if (s_fail) return;
         fence_proxy_alias();
+
+        // 3. this rank's share of the unit through the switch; the last
+        //    multimem unit may reach past n into the slot's padding, which is
+        //    never copied out
+        const size_t units = (n + M::bytes - 1) / M::bytes;
+        const size_t lo = units * a.rank / a.P, hi = units * (a.rank + 1) / a.P;
+        for (size_t u = lo + threadIdx.x; u < hi; u += U * blockDim.x) {
+            typename M::V v[U];
+#pragma unroll
+            for (int q = 0; q < U; ++q)
+                if (u + q * blockDim.x < hi) v[q] = M::ld(slot_mc + (u + q * blockDim.x) * M::bytes);
+#pragma unroll
+            for (int q = 0; q < U; ++q)
+                if (u + q * blockDim.x < hi) M::st(slot_mc + (u + q * blockDim.x) * M::bytes, v[q]);
+        }
+
+        // 4. meet on B, 5. copy-out
+        __syncthreads();
+        if (threadIdx.x == 0 && !nvls_meet(a, ctr_b, target, b, 1)) s_fail = 1;
+        __syncthreads();
+        if (s_fail) return;
+        fence_proxy_alias();
+        cta_copy<T>(a.dst + off, slot_uc, n);
     }
+    if (threadIdx.x == 0) a.steps[b] = base + k;
 }
 
 // ---------------------------------------------------------------- fold
@@ -729,12 +798,12 @@ struct QueryNvls {
 
 struct LaunchNvls {
     const NvlsArgs &a;
-    int b, t;
+    int b;
     cudaStream_t s;
     bool ok = false;
     template <int OP, int EC> void operator()() {
         if constexpr (Mm<OP, EC>::ok) {
-            nvls_kernel<OP, EC><<<b, t, 0, s>>>(a);
+            nvls_kernel<OP, EC><<<b, 512, 0, s>>>(a);
             ok = true;
         }
     }
@@ -810,10 +879,21 @@ int nvls_supported(int op, int ec) {
     return q.ok;
 }
 
-cudaError_t launch_nvls(int op, int ec, const NvlsArgs &a, int blocks, int threads, cudaStream_t s) {
-    LaunchNvls l{a, blocks, threads, s};
+cudaError_t launch_nvls(int op, int ec, const NvlsArgs &a, int blocks, cudaStream_t s) {
+    LaunchNvls l{a, blocks, s};
     if (!dispatch_op_class(op, ec, l) || !l.ok) return cudaErrorInvalidValue;
     return cudaGetLastError();
+}
+
+int nvls_max_ctas(int sm_count) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, nvls_kernel<CAIL_SUM, CAIL_EC_F32>, 512, 0) !=
+            cudaSuccess ||
+        per_sm < 1)
+        per_sm = 1;
+    if (per_sm > 2) per_sm = 2;
+    const int g = per_sm * (sm_count > 0 ? sm_count : 148);
+    return g > kMaxBlocks ? kMaxBlocks : g;
 }
 
 cudaError_t launch_copy(char *dst, const char *src, size_t bytes, int sm_count, cudaStream_t s) {

@@ -11,11 +11,12 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxBlocks = 512;           // flag slots per (source rank) and barrier kind
 constexpr int kFlagWords = kMaxRanks * kMaxBlocks;
 
-// Device-side error report (host-mapped).  code: 0 ok, 1 barrier timeout.
+// Device-side error report (host-mapped).  code: 0 ok, 1 barrier timeout,
+// 2 argument check failed (CAIL_DEVICE_CHECKS; waited_on holds the check).
 struct DevStatus {
     int code;
     int rank;       // rank whose kernel gave up
-    int waited_on;  // peer it was waiting for
+    int waited_on;  // peer it was waiting for (code 2: the failed check)
     int block;
     unsigned int epoch;
     unsigned int seen;
@@ -39,6 +40,7 @@ struct OneShotArgs {
     uint32_t epoch;
     unsigned long long timeout_ns;
     DevStatus *status;
+    int checks;                      // validate the arguments first (CAIL_DEVICE_CHECKS)
 };
 
 // Two-shot over registered user buffers: rank r reduces slice r of the
@@ -77,6 +79,12 @@ struct TwoShotArgs {
 // buffers are free for reuse as soon as the kernel has finished.
 // A launch may run several ranks' CTAs (the one-GPU emulation used by the
 // tests): CTA i belongs to rank rank0 + i / G and is CTA i % G of that rank.
+// With checks set, every CTA first validates the arguments (rank and CTA
+// counts against the grid, piece alignment, slot bounds against the area,
+// the slice table, round coverage, pointer alignment) and, if one fails,
+// reports DevStatus code 2 with the check's number and returns before it
+// touches memory or waits on a flag; every CTA sees the same arguments, so
+// all of them return.
 constexpr int kRsFlagBase = kFlagWords;      // word offsets in the flag array
 constexpr int kAgFlagBase = 2 * kFlagWords;
 struct PushArgs {
@@ -93,38 +101,48 @@ struct PushArgs {
     int vec;                         // every user buffer is 16-byte aligned
     unsigned long long timeout_ns;
     DevStatus *status;
+    size_t area;                     // bytes of each RS / AG area (bounds of the slots)
+    int checks;                      // validate the arguments first (CAIL_DEVICE_CHECKS)
 };
 
-// Pipelined NVLS allreduce of a whole message.  The message is cut into
-// sub-chunks that flow through a ring of 3 staging slots in a
-// multicast-bound region.  Iteration k (k = 0 .. K+1) copies sub-chunk k into
-// this rank's slot k%3, reduces this rank's slice of sub-chunk k-1 with
-// multimem.ld_reduce through the multicast view and broadcasts it with
-// multimem.st, and copies sub-chunk k-2 out of its slot; then all CTAs of
-// all ranks meet at a barrier.  With 3 slots, every slot's previous readers
-// and writers are done before the barrier that precedes its reuse.  The
-// barrier has two levels: CTAs arrive on a counter local to their GPU
-// (complete at local0 + (k + 1) * gridDim.x); the last arrival adds 1 to a
-// counter in the multicast region on every GPU (multimem.red); iteration k
-// is complete when the local copy of that counter reaches
-// target0 + (k + 1) * P.  Copy work and multimem work run on disjoint CTAs.
-constexpr int kNvlsSlots = 3;
+// NVLS allreduce through NVSwitch multicast, one independent pipeline per
+// CTA.  The message is cut into units of `unit` bytes; CTA b handles units
+// b, b + G, b + 2G, ... and owns one staging slot of `unit` bytes in the
+// multicast-bound region of every GPU.  For each of its units it
+//   1. copies the unit from the input into its slot (local HBM),
+//   2. meets CTA b of every other rank: fence, one multimem.red.release that
+//      adds 1 to its counter A[b] on every GPU, then waits until this GPU's
+//      copy of A[b] shows all P arrivals for this step,
+//   3. reduces this rank's 1/P of the unit with multimem.ld_reduce through
+//      the multicast view and broadcasts it with multimem.st,
+//   4. meets the others again on counter B[b] (every rank's share is now in
+//      every GPU's slot),
+//   5. copies the reduced unit from its slot into the output.
+// Different CTA indices never wait on one another, so the copies of some
+// CTAs overlap the multimem traffic of others without a grid-wide barrier.
+// One slot per CTA suffices: a rank refills its slot (step k + 1) only after
+// barrier B of step k, and the peers touch it again only after barrier A of
+// step k + 1, which needs that refill.  Counters only grow: steps[b] (this
+// GPU's unicast memory, the same on every GPU) holds the steps CTA b has
+// completed in earlier calls, so step k of this call is complete at
+// (steps[b] + k + 1) * P arrivals.  Counters are kNvlsCtrStride bytes apart.
+constexpr int kNvlsCtrStride = 128;
+constexpr size_t kNvlsCtrBytes = 2 * (size_t)kMaxBlocks * kNvlsCtrStride;  // A and B counters
 struct NvlsArgs {
     const char *src;                 // this rank's input (user buffer)
     char *dst;                       // this rank's output (user buffer)
-    char *uc;                        // unicast view of slot 0 (slots are slot_bytes apart)
+    char *uc;                        // unicast view of slot 0 (slot b at uc + b * unit)
     char *mc;                        // multicast view of slot 0
-    uint32_t *mc_counter;            // multicast view of the cross-rank counter
-    const uint32_t *uc_counter;      // this rank's unicast view of that counter
-    uint32_t *local_counter;         // this GPU's arrival counter (unicast only)
-    size_t count;                    // elements in the message
-    size_t sub;                      // elements per sub-chunk (sub * size is a multiple of 16)
-    size_t slot_bytes;
+    char *mc_ctr;                    // multicast view of the counters (A[b], then B[b])
+    const char *uc_ctr;              // this GPU's unicast view of the counters
+    uint32_t *steps;                 // per-CTA completed steps (unicast, kMaxBlocks words)
+    size_t bytes;                    // message bytes
+    size_t unit;                     // bytes per CTA and step (a multiple of 16)
+    size_t area;                     // bytes of the staging region (bounds of the slots)
     int P, rank;
-    int copy_blocks;                 // CTAs [0, copy_blocks) copy, the rest reduce
-    uint32_t target0, local0;
     unsigned long long timeout_ns;
     DevStatus *status;
+    int checks;                      // validate the arguments first (CAIL_DEVICE_CHECKS)
 };
 
 // Rank-order fold of P local sources into dst: dst = src[0] op src[1] op ...
@@ -143,7 +161,9 @@ cudaError_t launch_oneshot(int op, int ec, const OneShotArgs &a, int blocks, int
                            cudaStream_t s);
 cudaError_t launch_twoshot(int op, int ec, const TwoShotArgs &a, int blocks, int threads,
                            cudaStream_t s);
-cudaError_t launch_nvls(int op, int ec, const NvlsArgs &a, int blocks, int threads, cudaStream_t s);
+cudaError_t launch_nvls(int op, int ec, const NvlsArgs &a, int blocks, cudaStream_t s);
+// CTAs of the NVLS kernel that are co-resident on one GPU (512 threads each).
+int nvls_max_ctas(int sm_count);
 cudaError_t launch_fold(int op, int ec, const FoldArgs &a, int blocks, int threads, cudaStream_t s);
 // Push two-shot: a.G * ranks CTAs of 512 threads, where ranks = 1 in
 // production; cooperative = true launches it as a cooperative kernel (the

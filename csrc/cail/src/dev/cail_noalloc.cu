@@ -12,6 +12,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <mutex>
+
 #include "../core/cail_internal.h"
 #include "../gpu/cail_ops.h"
 #include "cail_noalloc.h"
@@ -98,21 +100,31 @@ struct Launch {
 };
 
 constexpr int kMaxDevices = 64;
+std::once_flag g_scratch_once[kMaxDevices];
 char *g_scratch_ptr[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device, looked up once
-// per device (set-up on the first call).  nullptr on failure.
+// Device address of the scratch array on device `dev` (the current device),
+// looked up once per device: the first call on a device does the set-up,
+// with std::call_once so that concurrent first calls from several host
+// threads neither race nor repeat it.  nullptr on failure.
 char *noalloc_scratch_of(int dev) {
     if (dev < 0 || dev >= kMaxDevices) return nullptr;
-    if (!g_scratch_ptr[dev]) {
-        void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess) {
-            CAIL_ERR("cail_reduce_sources_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-                     cudaGetErrorString(e));
-            return nullptr;
-        }
-        g_scratch_ptr[dev] = (char *)p;
+    // a failed lookup throws out of call_once, which leaves the flag unset,
+    // so a later call tries again
+    try {
+        std::call_once(g_scratch_once[dev], [dev] {
+            void *p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess) {
+                CAIL_ERR("cail_reduce_sources_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                         cudaGetErrorString(e));
+                cudaGetLastError();
+                throw e;
+            }
+            g_scratch_ptr[dev] = (char *)p;
+        });
+    } catch (cudaError_t) {
+        return nullptr;
     }
     return g_scratch_ptr[dev];
 }
@@ -126,13 +138,15 @@ extern "C" int cail_reduce_sources_noalloc(const void *const *srcs, int nsrc, vo
     if (dt == CAIL_INVALID) return MPI_ERR_TYPE;
     if (o == CAIL_OP_INVALID) return MPI_ERR_OP;
     if (!srcs || !dst) return MPI_ERR_ARG;
-    const size_t bytes = count * (size_t)cail_type_size(dt);
-    if (nsrc < 1 || nsrc > kMaxSrc || bytes > kSlot) {
-        CAIL_ERR("cail_reduce_sources_noalloc: %d sources of %zu bytes exceed the limit of %d sources "
-                 "of %zu bytes each",
-                 nsrc, bytes, kMaxSrc, kSlot);
+    const size_t esz = (size_t)cail_type_size(dt);
+    // compared as a count first, so that count * esz cannot wrap
+    if (nsrc < 1 || nsrc > kMaxSrc || count > kSlot / esz) {
+        CAIL_ERR("cail_reduce_sources_noalloc: %d sources of %zu elements of %zu bytes exceed the limit of %d "
+                 "sources of %zu bytes each",
+                 nsrc, count, esz, kMaxSrc, kSlot);
         return MPI_ERR_COUNT;
     }
+    const size_t bytes = count * esz;
     if (count == 0) return MPI_SUCCESS;
     Args a = {};
     for (int q = 0; q < nsrc; ++q) {

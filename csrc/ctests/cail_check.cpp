@@ -7,7 +7,7 @@
 // compared with PMPI_Allreduce of the same inputs (integers bit-exact,
 // floats bit-exact or within a reassociation tolerance, see --tol).
 //
-//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest|expect_error|memkinds|nan
+//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest|expect_error|stall|memkinds|nan
 //              [-c count] [-d] [-a algo]
 //              [-p] [-r reps] [--bits]
 //     -d      device buffers (cudaMalloc) instead of malloc
@@ -349,6 +349,29 @@ void mode_memkinds() {
 // With a failure injected on one rank (CAIL_FI_TWOSHOT_FAIL), a large call
 // must return an error on every rank (none may hang or report success), and
 // so must the next call on the same communicator.
+// Rank 1 stalls on the host (3 s) before its call; the zero-copy two-shot
+// path must not wait for it forever: with CAIL_HOST_TIMEOUT_MS=1000 rank 0
+// gives up at its arrive barrier and returns an error, and rank 1, arriving
+// late, sees rank 0's error bit and returns an error without launching.
+void mode_stall(int count) {
+    Buf s(count * sizeof(float)), r(count * sizeof(float));
+    std::vector<float> h(count, 1.0f);
+    s.put(h.data());
+    if (g_rank == 1) sleep(3);
+    const double t0 = MPI_Wtime();
+    const int rc = MPI_Allreduce(s.p, r.p, count, MPI_FLOAT, MPI_SUM, MPI_COMM_WORLD);
+    const double dt = MPI_Wtime() - t0;
+    report(rc != MPI_SUCCESS, "a call whose peer stalls on the host returns an error");
+    if (g_rank == 0) {
+        report(dt > 0.5 && dt < 2.5, "the waiting rank gives up at the host timeout");
+        printf("STALL DETECTED after %.2f s\n", dt);
+    } else {
+        report(dt < 2.0, "the late rank returns at once");
+    }
+    const int rc2 = MPI_Allreduce(s.p, r.p, count, MPI_FLOAT, MPI_SUM, MPI_COMM_WORLD);
+    report(rc2 != MPI_SUCCESS, "the broken communicator refuses the next call");
+}
+
 void mode_expect_error(int count) {
     Buf s(count * sizeof(float)), r(count * sizeof(float));
     std::vector<float> h(count, 1.0f);
@@ -607,6 +630,7 @@ int main(int argc, char **argv) {
     else if (mode == "leave") mode_leave(count ? count : 65536);
     else if (mode == "canary_selftest") mode_canary_selftest();
     else if (mode == "expect_error") mode_expect_error(count ? count : (1 << 20));
+    else if (mode == "stall") mode_stall(count ? count : (1 << 20));
     else if (mode == "memkinds") mode_memkinds();
     else if (mode == "nan") mode_nan();
     else { fprintf(stderr, "unknown mode %s\n", mode.c_str()); MPI_Abort(MPI_COMM_WORLD, 2); }

@@ -79,6 +79,7 @@ struct PushEmu {
             a.ag[q] = ws[q] + flags + area;
         }
         a.rank0 = 0;
+        a.area = area;
         a.epoch0 = epoch + 1;
         epoch += (uint32_t)a.rounds;
         a.timeout_ns = timeout_ns;
@@ -109,10 +110,14 @@ void shape(cail::PushArgs &a, int P, size_t count, size_t esz, bool vec, int G, 
 // elements of storage class ec, operator op: cail_elem_class_t and
 // cail_op_t values).  G CTAs per rank (0: as many as can be co-resident) and
 // `piece` bytes per CTA, round and slice (0: 32 KiB; a multiple of 16).
-// Returns 0, the device status code (1: a wait timed out), or -1 on a CUDA
-// or argument error.
+// options: bit 0 turns on the kernel's argument checks (CAIL_DEVICE_CHECKS);
+// bit 1 passes one round too few, an inconsistent argument that the checks
+// must catch (unchecked, the kernel would only leave the end of the longest
+// slice unreduced: it never reaches beyond its buffers).
+// Returns 0, the device status code (1: a wait timed out, 2: an argument
+// check failed), or -1 on a CUDA or argument error.
 extern "C" int cail_emulate_push(int P, const void *const *srcs, void *const *dsts, size_t count, int ec, int op,
-                                 int G, size_t piece, int calls) {
+                                 int G, size_t piece, int calls, int options) {
     if (P < 2 || P > cail::kMaxRanks || calls < 1 || !srcs || !dsts) return -1;
     static const int esz_of[CAIL_EC_NUM] = {1, 1, 2, 2, 4, 4, 8, 8, 4, 8};
     if (ec < 0 || ec >= CAIL_EC_NUM) return -1;
@@ -141,6 +146,8 @@ extern "C" int cail_emulate_push(int P, const void *const *srcs, void *const *ds
             a.dst[q] = (char *)dsts[q];
         }
         emu.args(a, P, 2000000000ull);
+        a.checks = options & 1;
+        if ((options & 2) && a.rounds > 1) a.rounds -= 1;
         if (cail::launch_push(op, ec, a, P, true, s) != cudaSuccess) rc = -1;
     }
     cail::DevStatus h;

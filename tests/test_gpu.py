@@ -98,6 +98,29 @@ def test_p2p_algorithms_device_buffers_one_gpu(algo, np):
     assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
 
 
+@pytest.mark.parametrize("copy_max", ["0", "134217728"], ids=["bulk_copy", "copy_kernel"])
+def test_single_rank_copy_unaligned_views(copy_max):
+    """One rank, byte buffers whose views start a few bytes off a 16-byte
+    boundary and have odd lengths: the copy's plain-load head and tail run;
+    the output must equal the input byte for byte, and the bytes around the
+    view must stay untouched."""
+    need_gpus(1)
+    code = ("import cail_b200 as c, torch; c.init();"
+            "ok = True\n"
+            "for off, n in ((3, 1000003), (13, 65), (5, 7), (1, (3 << 20) + 11)):\n"
+            "    src = torch.randint(0, 256, (n + 64,), dtype=torch.uint8, device='cuda')\n"
+            "    dst = torch.full((n + 64,), 7, dtype=torch.uint8, device='cuda')\n"
+            "    c.ops.allreduce(src[off:off + n], dst[off:off + n], op='max')\n"
+            "    torch.cuda.synchronize()\n"
+            "    ok = ok and torch.equal(dst[off:off + n], src[off:off + n])\n"
+            "    ok = ok and bool((dst[:off] == 7).all()) and bool((dst[off + n:] == 7).all())\n"
+            "print('views ok', ok, c.last_algorithm()); c.finalize()")
+    env = dict(os.environ, CAIL_COPY_KERNEL_MAX=copy_max, CAIL_MIN_MSG_SIZE="0")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "views ok True copy" in r.stdout, r.stdout + r.stderr
+
+
 def test_device_wait_timeout_reports_status():
     """A one-shot kernel whose peer never arrives gives up after the limit
     and reports code 1; the context stays usable afterwards."""
@@ -131,28 +154,36 @@ def nranks():
     return [n for n in cand if n <= gpu_count()]
 
 
+def algo_env(algo):
+    """CAIL_ALGO for a test parameter; two_shot_zerocopy is two_shot over the
+    user buffers (CAIL_TWOSHOT_ZEROCOPY=1) instead of the push kernel."""
+    if algo == "two_shot_zerocopy":
+        return {"CAIL_ALGO": "two_shot", "CAIL_TWOSHOT_ZEROCOPY": "1"}
+    return {"CAIL_ALGO": algo}
+
+
 @pytest.mark.multigpu
-@pytest.mark.parametrize("algo", ["one_shot", "two_shot", "ce_two_shot"])
+@pytest.mark.parametrize("algo", ["one_shot", "two_shot", "two_shot_zerocopy", "ce_two_shot"])
 def test_nvlink_p2p_matrix_bit_exact(algo):
     # counts {1,2,3,4099,4100,4102}: heads, tails, fewer elements than ranks;
     # separate and in place; floats bit-identical to the rank-order oracle
     need_gpus(2)
     for np in nranks():
         r = mpirun(np, ["cail_check", "-m", "matrix", "-c", "4099", "-d", "-p", "--bits"], preload="cuda",
-                   env={"CAIL_ALGO": algo, "CAIL_MIN_MSG_SIZE": "0"}, timeout=1200)
+                   env={**algo_env(algo), "CAIL_MIN_MSG_SIZE": "0"}, timeout=1200)
         assert ok(r), f"np={np}\n" + r.stdout[-3000:] + r.stderr[-3000:]
 
 
 @pytest.mark.multigpu
-@pytest.mark.parametrize("algo", ["auto", "nvls", "two_shot", "ce_two_shot"])
+@pytest.mark.parametrize("algo", ["auto", "nvls", "two_shot", "two_shot_zerocopy", "ce_two_shot"])
 def test_nvlink_config3_coverage(algo):
     """20 datatypes x SUM/PROD/MAX/MIN at counts 1,000,003 and 4,194,304 at
     every available rank count; integers bit-exact, floats within
     reassociation tolerance (NVLS) or bit-exact (two-shot, both kinds)."""
     need_gpus(2)
     for np in nranks():
-        args = ["cail_check", "-m", "config3", "-d"] + (["--bits"] if algo in ("two_shot", "ce_two_shot") else ["--tol", "1e-4"])
-        r = mpirun(np, args, preload="cuda", env={"CAIL_ALGO": algo}, timeout=1200)
+        args = ["cail_check", "-m", "config3", "-d"] + (["--bits"] if "two_shot" in algo else ["--tol", "1e-4"])
+        r = mpirun(np, args, preload="cuda", env=algo_env(algo), timeout=1200)
         assert ok(r), f"np={np} algo={algo}\n" + r.stdout[-3000:] + r.stderr[-3000:]
 
 
@@ -206,14 +237,16 @@ def test_stream_ordered_small_messages_bit_exact():
 
 @pytest.mark.multigpu
 def test_two_shot_failure_on_one_rank_reaches_every_rank():
-    """A failure injected on the host of rank 1 (its import of the peers'
+    """Zero-copy two-shot (CAIL_TWOSHOT_ZEROCOPY=1), the path with a host
+    exchange: a failure injected on the host of rank 1 (its import of the peers'
     buffers fails, as a failing cudaIpcOpenMemHandle would) must end the
     two-shot call with an error on every rank: rank 1 still passes both host
     barriers with an error bit, so rank 0 neither waits forever nor returns
     a result whose slice 1 was never reduced.  No GPU fault is involved."""
     need_gpus(2)
     r = mpirun(2, ["cail_check", "-m", "expect_error", "-d"], preload="cuda",
-               env={"CAIL_ALGO": "two_shot", "CAIL_FI_TWOSHOT_FAIL": "1", "CAIL_NVLS": "0"}, timeout=300)
+               env={"CAIL_ALGO": "two_shot", "CAIL_TWOSHOT_ZEROCOPY": "1", "CAIL_FI_TWOSHOT_FAIL": "1",
+                    "CAIL_NVLS": "0"}, timeout=300)
     assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
     assert "injected import failure" in r.stderr
     assert "a peer failed during the call" in r.stderr
@@ -226,3 +259,18 @@ def test_rank_leaving_between_steps_is_detected():
                env={"CAIL_NVLS": "0", "NCCL_NVLS_ENABLE": "0", "CAIL_DEVICE_TIMEOUT_MS": "1000"}, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "LEAVE DETECTED at step 2" in r.stdout
+
+
+@pytest.mark.multigpu
+def test_host_barrier_wait_is_bounded():
+    """Zero-copy two-shot with a peer that stalls on the host (alive, but 3 s
+    late): the waiting rank returns an error after CAIL_HOST_TIMEOUT_MS, the
+    late rank sees the error bit and returns at once, and the communicator
+    refuses further calls.  No GPU is involved in the stall."""
+    need_gpus(2)
+    r = mpirun(2, ["cail_check", "-m", "stall", "-d"], preload="cuda",
+               env={"CAIL_ALGO": "two_shot", "CAIL_TWOSHOT_ZEROCOPY": "1", "CAIL_HOST_TIMEOUT_MS": "1000",
+                    "CAIL_NVLS": "0"}, timeout=300)
+    assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+    assert "STALL DETECTED" in r.stdout
+    assert "did not reach the arrive barrier" in r.stderr

@@ -34,7 +34,8 @@ def _lib():
     k = ctypes.CDLL(os.path.join(LIB, "libcail_kbench.so"))
     vp = ctypes.c_void_p
     k.cail_emulate_push.argtypes = [ctypes.c_int, ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.c_size_t,
-                                    ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_int]
+                                    ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_int,
+                                    ctypes.c_int]
     k.cail_bench_kernel_local.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_int,
                                           ctypes.POINTER(ctypes.c_float)]
     return k
@@ -80,7 +81,7 @@ def _signed_view(dt):
     return {np.uint16: np.int16, np.uint32: np.int32, np.uint64: np.int64}.get(dt, dt)
 
 
-def _run(k, P, xs, op_i, ec, offset=0, in_place=False, G=0, piece=0, calls=2):
+def _run(k, P, xs, op_i, ec, offset=0, in_place=False, G=0, piece=0, calls=2, options=1, expect_rc=0):
     """Uploads xs (one array per rank) at `offset` elements into fresh device
     buffers, runs the emulated push two-shot and returns the P outputs."""
     import torch
@@ -105,9 +106,9 @@ def _run(k, P, xs, op_i, ec, offset=0, in_place=False, G=0, piece=0, calls=2):
     vp = ctypes.c_void_p
     sa = (vp * P)(*[s.data_ptr() for s in srcs])
     da = (vp * P)(*[d.data_ptr() for d in dsts])
-    rc = k.cail_emulate_push(P, sa, da, n, ec, op_i, G, piece, 1 if in_place else calls)
+    rc = k.cail_emulate_push(P, sa, da, n, ec, op_i, G, piece, 1 if in_place else calls, options)
     torch.cuda.synchronize()
-    assert rc == 0, f"cail_emulate_push returned {rc}"
+    assert rc == expect_rc, f"cail_emulate_push returned {rc}"
     return [d.cpu().numpy().view(dt) for d in dsts]
 
 
@@ -148,6 +149,22 @@ def test_push_two_shot_emulated_many_rounds():
         want = _fold(xs, "sum")
         for got in _run(k, P, xs, 0, 8, G=G, piece=piece, calls=3):
             assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (P, G, piece)
+
+
+def test_device_checks_catch_an_inconsistent_argument():
+    """CAIL_DEVICE_CHECKS: one round too few for the message (harmless
+    unchecked: the end of the longest slice would stay unreduced) is caught
+    before the kernel touches memory: status code 2, the outputs untouched
+    (still 7), and the context usable for a correct call afterwards."""
+    k = _lib()
+    rng = np.random.default_rng(11)
+    xs = _inputs(rng, np.float32, "sum", 4, 100000)
+    outs = _run(k, 4, xs, 0, 8, G=2, piece=4096, calls=1, options=3, expect_rc=2)
+    for got in outs:
+        assert (got == 7).all()
+    want = _fold(xs, "sum")
+    for got in _run(k, 4, xs, 0, 8, G=2, piece=4096, calls=1, options=1):
+        assert np.array_equal(got.view(np.uint8), want.view(np.uint8))
 
 
 @pytest.mark.parametrize("kernel", [3, 5], ids=["bulk_copy", "copy"])
