@@ -126,7 +126,6 @@ static_assert(3 * cail::kFlagWords * sizeof(uint32_t) <= kFlagBytes, "flag array
 constexpr size_t kSlotBytes = 1 << 20;                  // one-shot: bytes per source slot
 constexpr size_t kScratchParity = kMaxRanks * kSlotBytes;  // one slot per source rank
 constexpr size_t kPushOff = kFlagBytes + 2 * kScratchParity;  // push two-shot: RS area, then AG area
-constexpr size_t kDefaultPieceMax = 32 << 10;           // push two-shot: bytes per CTA, round and slice
 constexpr size_t kDefaultPieceMin = 4 << 10;
 constexpr size_t kNvlsStepsOff = 3 * cail::kFlagWords * sizeof(uint32_t);  // NVLS per-CTA steps, in the flag area
 static_assert(kNvlsStepsOff + cail::kMaxBlocks * sizeof(uint32_t) <= kFlagBytes, "flag area too small");
@@ -689,7 +688,7 @@ size_t env_bytes(const char *name, size_t dflt, size_t lo, size_t hi) {
     return v < lo ? lo : (v > hi ? hi : v);
 }
 size_t push_piece_max_env() {
-    static const size_t v = env_bytes("CAIL_TWOSHOT_PIECE_MAX", kDefaultPieceMax, 1024, (size_t)1 << 20);
+    static const size_t v = env_bytes("CAIL_TWOSHOT_PIECE_MAX", 0, 1024, (size_t)1 << 20);
     return v;
 }
 size_t push_piece_min_env() {
@@ -748,9 +747,17 @@ cail_dev_comm *create_context(MPI_Comm comm) {
     ok = cudaStreamCreateWithFlags(&dc->stream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&dc->legacy_ev, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&dc->done_ev, cudaEventDisableTiming) == cudaSuccess;
-    // push two-shot areas: 2 parities x G CTAs x P sources x the largest piece
+    // push two-shot areas: 2 parities x G CTAs x P sources x the largest piece;
+    // by default the piece keeps the two areas near 296 MiB (128 KiB at 2
+    // ranks, 64 KiB at 4, 32 KiB at 8): larger pieces amortise the flag
+    // round trips of each round
     dc->push_gmax = cail::push_max_ctas(1, dc->sms);
     dc->push_piece_max = push_piece_max_env();
+    if (dc->push_piece_max == 0) {
+        size_t pm = ((size_t)296 << 20) / ((size_t)4 * dc->push_gmax * dc->P);
+        pm = pm / (16 << 10) * (16 << 10);
+        dc->push_piece_max = std::min(std::max(pm, (size_t)16 << 10), (size_t)256 << 10);
+    }
     dc->push_area = ((size_t)2 * dc->push_gmax * dc->P * dc->push_piece_max + 255) / 256 * 256;
     ok = ok && cudaMalloc(&dc->ws, kPushOff + 2 * dc->push_area) == cudaSuccess;
     ok = ok && cudaMemset(dc->ws, 0, kFlagBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;

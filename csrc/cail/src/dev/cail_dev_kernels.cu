@@ -378,14 +378,13 @@ __global__ void __launch_bounds__(512, 2) push_kernel(PushArgs a) {
     const char *src = a.src[me];
     char *dst = a.dst[me];
     const size_t slot_stride = a.piece;
-    for (int k = 0; k < a.rounds; ++k) {
-        const size_t ob = ((size_t)k * a.G + b) * a.piece;
-        if (ob >= a.max_slice) break;  // the same on every rank
+    auto round_off = [&](int k) { return ((size_t)k * a.G + b) * a.piece; };
+    // 1. reduce-scatter by pushes: the pieces of round k of every other
+    //    rank's slice -> that rank's RS slot, then one flag per peer
+    auto push_rs = [&](int k) {
+        const size_t ob = round_off(k);
         const uint32_t e = a.epoch0 + (uint32_t)k;
-        const size_t par = e & 1u;
-        const size_t my_slot = ((par * a.G + b) * P + me) * slot_stride;
-
-        // 1. reduce-scatter by pushes: piece of slice q -> rank q
+        const size_t my_slot = (((e & 1u) * a.G + b) * P + me) * slot_stride;
         for (int q = 0; q < P; ++q) {
             if (q == me) continue;
             const size_t n = push_piece_len(a, q, ob);
@@ -393,6 +392,14 @@ __global__ void __launch_bounds__(512, 2) push_kernel(PushArgs a) {
         }
         __syncthreads();
         push_signal(a, me, b, kRsFlagBase, e);
+    };
+    if (round_off(0) < a.max_slice) push_rs(0);
+    for (int k = 0; k < a.rounds; ++k) {
+        const size_t ob = round_off(k);
+        if (ob >= a.max_slice) break;  // the same on every rank
+        const uint32_t e = a.epoch0 + (uint32_t)k;
+        const size_t par = e & 1u;
+        const size_t my_slot = ((par * a.G + b) * P + me) * slot_stride;
         push_wait(a, me, b, kRsFlagBase, e, &s_fail);
         __syncthreads();
         if (s_fail) return;
@@ -438,6 +445,13 @@ __global__ void __launch_bounds__(512, 2) push_kernel(PushArgs a) {
         }
         __syncthreads();
         push_signal(a, me, b, kAgFlagBase, e);
+
+        // look ahead: round k + 1's reduce-scatter goes out before this
+        // round's gather is waited for.  Its RS slots (the parity of round
+        // k - 1) are free: each peer raised AG for round k - 1, which this CTA
+        // received in the previous iteration, only after it had folded them.
+        if (k + 1 < a.rounds && round_off(k + 1) < a.max_slice) push_rs(k + 1);
+
         push_wait(a, me, b, kAgFlagBase, e, &s_fail);
         __syncthreads();
         if (s_fail) return;

@@ -72,9 +72,12 @@ struct TwoShotArgs {
 //   3. it waits for every peer's AG[q][b] and copies the gathered pieces of
 //      the other slices from its AG slots into its output.
 // Epochs grow by one per round, so flags never need resetting, and slots
-// alternate between two parities: round k + 2 of a CTA starts only after it
-// has received the peers' AG pieces of round k + 1, which each peer sends
-// after it finished reading its slots of round k.  No rank reads or writes
+// alternate between two parities.  A CTA pushes round k + 1's pieces (step 1)
+// right after it raised AG for round k, before it waits for the peers' AG of
+// round k: those RS slots (round k - 1's parity) are free because every peer
+// raised AG for round k - 1 only after folding them.  Its AG pieces of round
+// k go out after it received the peers' RS pieces of round k, which each
+// peer sends after it finished copying out its AG slots of round k - 2.  No rank reads or writes
 // another rank's user buffers, so the call needs no host barrier and the
 // buffers are free for reuse as soon as the kernel has finished.
 // A launch may run several ranks' CTAs (the one-GPU emulation used by the

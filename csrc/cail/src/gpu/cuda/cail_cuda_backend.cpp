@@ -129,7 +129,7 @@ int cail_gpu_synchronize(void) { return sync_or_warn("gpu_synchronize"); }
 
 // One rank: the reference copies with cudaMemcpy and synchronises the legacy
 // stream (src/gpu/cuda/cail_cuda_mem.c:29-34 there).  Here: cail's copy
-// kernel up to CAIL_COPY_KERNEL_MAX bytes (default 128 MiB), the TMA
+// kernel up to CAIL_COPY_KERNEL_MAX bytes (default 96 MiB), the TMA
 // bulk-copy kernel above it.  Measured on B200: 0.0237 ms for 64 MiB with
 // the copy kernel against 0.0292 ms for cudaMemcpyAsync, and 0.326 ms per
 // GiB with the bulk copy against 0.333 ms; a blocking call of 32 KiB costs
@@ -139,7 +139,7 @@ int cail_gpu_single_rank(const void *src, void *dst, size_t bytes) {
     if (src == dst || bytes == 0) return 0;
     static const size_t kernel_max = [] {
         const char *e = getenv("CAIL_COPY_KERNEL_MAX");
-        return e && *e ? (size_t)strtoull(e, nullptr, 10) : ((size_t)128 << 20);
+        return e && *e ? (size_t)strtoull(e, nullptr, 10) : ((size_t)96 << 20);
     }();
     const int d = current_device();
     cudaStream_t s = stream();

@@ -357,6 +357,9 @@ void mode_stall(int count) {
     Buf s(count * sizeof(float)), r(count * sizeof(float));
     std::vector<float> h(count, 1.0f);
     s.put(h.data());
+    // one call first: the communicator's device setup is collective and would
+    // absorb the stall
+    report(MPI_Allreduce(s.p, r.p, count, MPI_FLOAT, MPI_SUM, MPI_COMM_WORLD) == MPI_SUCCESS, "warm-up call");
     if (g_rank == 1) sleep(3);
     const double t0 = MPI_Wtime();
     const int rc = MPI_Allreduce(s.p, r.p, count, MPI_FLOAT, MPI_SUM, MPI_COMM_WORLD);
