@@ -46,7 +46,9 @@ def dram_bytes(kernel: str, P: int, nbytes: int) -> int:
     if kernel == "fold":
         return (P + 1) * nbytes                 # P sources, one output
     if kernel == "one_shot":
-        return nbytes + P * nbytes + P * nbytes + nbytes   # read src, push P slots, fold P, write dst
+        # all P emulated ranks: each reads its input once, stores it into
+        # P - 1 peers' slots, folds P copies and writes its output
+        return P * (2 * P + 1) * nbytes
     if kernel == "two_shot_zerocopy":
         return 2 * nbytes                       # its slice of P inputs read, of P outputs written (x P / P)
     if kernel == "push":

@@ -121,14 +121,16 @@ void load_driver() {
 }
 
 // ---------------------------------------------------------------- constants
-constexpr size_t kFlagBytes = 64 << 10;                 // flags: one-shot, push RS, push AG (48 KiB used)
-static_assert(3 * cail::kFlagWords * sizeof(uint32_t) <= kFlagBytes, "flag arrays exceed the flag area");
-constexpr size_t kSlotBytes = 1 << 20;                  // one-shot: bytes per source slot
-constexpr size_t kScratchParity = kMaxRanks * kSlotBytes;  // one slot per source rank
-constexpr size_t kPushOff = kFlagBytes + 2 * kScratchParity;  // push two-shot: RS area, then AG area
-constexpr size_t kDefaultPieceMin = 4 << 10;
-constexpr size_t kNvlsStepsOff = 3 * cail::kFlagWords * sizeof(uint32_t);  // NVLS per-CTA steps, in the flag area
-static_assert(kNvlsStepsOff + cail::kMaxBlocks * sizeof(uint32_t) <= kFlagBytes, "flag area too small");
+// Workspace of a rank (IPC-exported): [flag area | one-shot area | push RS
+// area | push AG area].  The flag area holds the one-shot, RS and AG flags
+// (one word per source rank and CTA each) and the per-CTA round / step
+// counters of the one-shot and NVLS kernels.
+constexpr size_t kFlagBytes = 64 << 10;
+static_assert(cail::kFlagAreaWords * sizeof(uint32_t) <= kFlagBytes, "flag arrays exceed the flag area");
+constexpr size_t kOsOff = kFlagBytes;
+constexpr size_t kDefaultPieceMin = 4 << 10;             // push two-shot: smallest piece
+constexpr size_t kOsPieceMin = 8 << 10;                  // one-shot: smallest piece
+constexpr size_t kNvlsStepsOff = cail::kNvlsStepsBase * sizeof(uint32_t);
 constexpr size_t kNvlsCtrRegion = (cail::kNvlsCtrBytes + 65535) / 65536 * 65536;  // counters, then staging
 constexpr size_t kDefaultNvlsUnit = 256 << 10;          // NVLS: largest bytes per CTA and step
 
@@ -225,6 +227,8 @@ struct cail_dev_comm {
     int push_gmax = 0;
     size_t push_piece_max = 0, push_area = 0;
     uint32_t push_epoch = 0;
+    // one-shot: largest piece and bytes of its area
+    size_t os_piece_max = 0, os_area = 0;
     DevStatus *status_h = nullptr, *status_d = nullptr;
     // host exchange
     XSlot *xs = nullptr;
@@ -759,7 +763,15 @@ cail_dev_comm *create_context(MPI_Comm comm) {
         dc->push_piece_max = std::min(std::max(pm, (size_t)16 << 10), (size_t)256 << 10);
     }
     dc->push_area = ((size_t)2 * dc->push_gmax * dc->P * dc->push_piece_max + 255) / 256 * 256;
-    ok = ok && cudaMalloc(&dc->ws, kPushOff + 2 * dc->push_area) == cudaSuccess;
+    // one-shot area: 3 slots x G CTAs x P sources x the largest piece, about
+    // 112 MiB (64 KiB pieces at 2 ranks, 16 KiB at 8)
+    {
+        size_t pm = ((size_t)112 << 20) / ((size_t)cail::kOsSlots * dc->push_gmax * dc->P);
+        pm = pm / (8 << 10) * (8 << 10);
+        dc->os_piece_max = std::min(std::max(pm, kOsPieceMin), (size_t)256 << 10);
+        dc->os_area = ((size_t)cail::kOsSlots * dc->push_gmax * dc->P * dc->os_piece_max + 255) / 256 * 256;
+    }
+    ok = ok && cudaMalloc(&dc->ws, kOsOff + dc->os_area + 2 * dc->push_area) == cudaSuccess;
     ok = ok && cudaMemset(dc->ws, 0, kFlagBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
     ok = ok && cudaHostAlloc((void **)&dc->status_h, sizeof(DevStatus), cudaHostAllocMapped) == cudaSuccess;
     ok = ok && cudaHostGetDevicePointer((void **)&dc->status_d, dc->status_h, 0) == cudaSuccess;
@@ -846,55 +858,18 @@ int check_status(cail_dev_comm *dc, const char *what) {
 unsigned long long timeout_ns() { return (unsigned long long)cail_global_state.device_timeout_ms * 1000000ull; }
 
 // ---- one-shot
+// One launch for any size: pieces of at least 8 KiB so that small messages
+// use few CTAs (one vector per thread), at most the area's piece.
 int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec,
-                bool sync) {
-    const size_t bytes = count * esz;
-    cail::OneShotArgs a;
-    memset(&a, 0, sizeof(a));
-    a.src = src;
-    a.dst = dst;
-    a.count = count;
-    a.P = dc->P;
-    a.rank = dc->rank;
-    a.epoch = ++dc->epoch;
-    const size_t parity = (a.epoch & 1) ? kScratchParity : 0;
-    for (int q = 0; q < dc->P; ++q) {
-        a.slot_out[q] = dc->peer_ws[q] + kFlagBytes + parity + (size_t)dc->rank * kSlotBytes;
-        a.peer_flags[q] = (uint32_t *)dc->peer_ws[q];
-    }
-    a.slot_in = dc->ws + kFlagBytes + parity;
-    a.slot_bytes = kSlotBytes;
-    a.my_flags = (uint32_t *)dc->ws;
-    a.timeout_ns = timeout_ns();
-    a.status = dc->status_d;
-    a.checks = cail_global_state.device_checks;
-    // ~2 vectors per thread, 512 threads per block
-    size_t vec = (bytes + 15) / 16;
-    int threads = 512;
-    size_t want = (vec + 2 * threads - 1) / (2 * threads);
-    int blocks = (int)(want < 1 ? 1 : (want > (size_t)kMaxBlocks ? kMaxBlocks : want));
-    static const int forced_blocks = [] {
-        const char *e = getenv("CAIL_ONESHOT_BLOCKS");
-        int b = e ? atoi(e) : 0;
-        return (b >= 1 && b <= kMaxBlocks) ? b : 0;
-    }();
-    if (forced_blocks) blocks = forced_blocks;
-    double t = cail_global_state.profile ? cail_now_us() : 0.0;
-    cudaError_t e = cail::launch_oneshot(op, ec, a, blocks, threads, dc->stream);
-    cail_prof_mark(CAIL_PH_LAUNCH, t);
-    cail_counters.launches++;
-    if (e != cudaSuccess) {
-        CAIL_ERR("one_shot launch failed: %s", cudaGetErrorString(e));
-        return MPI_ERR_OTHER;
-    }
-    return sync ? check_status(dc, "one_shot") : MPI_SUCCESS;
-}
+                bool allow_ordered);
 
 // Stream-ordered completion (cail_set_stream_ordered): the legacy stream
 // waits for the call's kernels and the host returns at once.  This is safe
-// for the one-shot kernel alone: its scratch parity comes back two calls
-// later, and a rank's call k+2 can only start after every peer's call k has
-// finished (stream order on each GPU plus the peers' flags of call k+1).
+// for the one-shot, push two-shot and NVLS kernels, which need no host
+// exchange: each touches only its own workspace slots and its own user
+// buffers, and their per-CTA flag protocols order every reuse of a slot
+// across calls as within one call (successive calls run in stream order on
+// each GPU).
 bool stream_ordered_ok(const cail_dev_comm *dc) {
     return cail_global_state.stream_ordered && cail_global_state.stream_sync && dc->done_ev;
 }
@@ -923,13 +898,40 @@ int poll_pending(cail_dev_comm *dc) {
     return MPI_ERR_OTHER;
 }
 
-int run_oneshot_chunked(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz,
-                        int op, int ec, bool allow_ordered = false) {
-    size_t per = kSlotBytes / esz;
-    for (size_t off = 0; off < count; off += per) {
-        size_t n = count - off < per ? count - off : per;
-        int rc = run_oneshot(dc, src + off * esz, dst + off * esz, n, esz, op, ec, false);
-        if (rc != MPI_SUCCESS) return rc;
+int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec,
+                bool allow_ordered) {
+    const size_t bytes = count * esz;
+    cail::OneShotArgs a;
+    memset(&a, 0, sizeof(a));
+    const int gmax = dc->push_gmax;
+    size_t piece = (bytes + gmax - 1) / gmax;
+    piece = (piece + 15) / 16 * 16;
+    piece = std::min(std::max(piece, kOsPieceMin), dc->os_piece_max);
+    a.G = (int)std::max<size_t>(1, std::min<size_t>((bytes + piece - 1) / piece, (size_t)gmax));
+    a.piece = piece;
+    a.bytes = bytes;
+    a.area = dc->os_area;
+    a.P = dc->P;
+    a.rank0 = dc->rank;
+    a.vec = (((uintptr_t)src | (uintptr_t)dst) & 15) == 0 ? 1 : 0;
+    a.src[dc->rank] = src;
+    a.dst[dc->rank] = dst;
+    a.rounds_done[dc->rank] = (uint32_t *)dc->ws + cail::kOsRoundsBase;
+    for (int q = 0; q < dc->P; ++q) {
+        a.slots[q] = dc->peer_ws[q] + kOsOff;
+        a.flags[q] = (uint32_t *)dc->peer_ws[q];
+    }
+    a.timeout_ns = timeout_ns();
+    a.status = dc->status_d;
+    a.checks = cail_global_state.device_checks;
+    double t = cail_global_state.profile ? cail_now_us() : 0.0;
+    cudaError_t e = cail::launch_oneshot(op, ec, a, 1, false, dc->stream);
+    cail_prof_mark(CAIL_PH_LAUNCH, t);
+    cail_counters.launches++;
+    if (e != cudaSuccess) {
+        CAIL_ERR("one_shot launch failed: %s", cudaGetErrorString(e));
+        dc->broken = true;
+        return MPI_ERR_OTHER;
     }
     if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc);
     return check_status(dc, "one_shot");
@@ -974,8 +976,8 @@ int run_push(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
     a.src[dc->rank] = src;
     a.dst[dc->rank] = dst;
     for (int q = 0; q < dc->P; ++q) {
-        a.rs[q] = dc->peer_ws[q] + kPushOff;
-        a.ag[q] = dc->peer_ws[q] + kPushOff + dc->push_area;
+        a.rs[q] = dc->peer_ws[q] + kOsOff + dc->os_area;
+        a.ag[q] = dc->peer_ws[q] + kOsOff + dc->os_area + dc->push_area;
         a.flags[q] = (uint32_t *)dc->peer_ws[q];
     }
     a.epoch0 = dc->push_epoch + 1;
@@ -1176,7 +1178,7 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     if (!all_ok) {
         // some rank's buffer cannot be exported: every rank sees the same
         // descriptors and takes the copy-in path instead
-        rc = run_oneshot_chunked(dc, src, dst, count, esz, op, ec);
+        rc = run_oneshot(dc, src, dst, count, esz, op, ec, false);
     } else {
         cail::TwoShotArgs a;
         memset(&a, 0, sizeof(a));
@@ -1312,22 +1314,39 @@ int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
     return check_status(dc, "nvls");
 }
 
-// CAIL_TWOSHOT_ZEROCOPY=1: two_shot runs the zero-copy kernel over the user
-// buffers (host exchange and barriers) instead of the push kernel.
-bool twoshot_zero_copy() {
-    static const bool v = [] {
+// Which two-shot kernel runs for P ranks: the zero-copy kernel over the user
+// buffers (host exchange of their IPC handles, host barriers) or the push
+// kernel over the workspace (no host step).  CAIL_TWOSHOT_ZEROCOPY=1 / =0
+// forces one.  Measured on B200 (blocking calls, float sum), the zero-copy
+// kernel leads at every size from 128 KiB: at 2 ranks 20.2 vs 29.7 us at
+// 1 MiB and 659 vs 662 GB/s at 1 GiB; at 8 ranks 30.2 vs 38.5 us at 1 MiB,
+// 74.8 vs 102.6 us at 16 MiB and 650 vs 557 GB/s at 1 GiB.  Its host
+// barrier costs a few microseconds even with 8 processes, and it moves about
+// 2N bytes through HBM per rank against about 6N for the push kernel (which
+// stages through the workspace).  The push kernel runs when calls complete
+// in stream order (cail_set_stream_ordered), which a host barrier cannot.
+int twoshot_zero_copy_env() {
+    static const int v = [] {
         const char *e = getenv("CAIL_TWOSHOT_ZEROCOPY");
-        return e && *e && *e != '0';
+        return e && *e ? (*e != '0' ? 1 : 0) : -1;
     }();
     return v;
 }
 
-// Built-in one_shot / two_shot crossover (measured on B200 at 2 to 8 ranks:
-// one_shot is ahead up to 512 KiB).  CAIL_TUNE_FILE lines replace it per
-// rank count.
+bool twoshot_zero_copy(const cail_dev_comm *dc) {
+    const int env = twoshot_zero_copy_env();
+    if (env >= 0) return env == 1;
+    return !stream_ordered_ok(dc);
+}
+
+// Built-in one_shot / two_shot crossover per rank count, measured on B200
+// (blocking calls, float sum): 2 ranks, one-shot and zero-copy two-shot
+// equal up to 64 KiB (20.2 us), two-shot ahead from 128 KiB; 8 ranks,
+// one-shot ahead up to 256 KiB (28.2 vs 29.0 us), two-shot from 512 KiB
+// (27.8 vs 31.8 us).  CAIL_TUNE_FILE lines replace it per rank count.
 size_t default_oneshot_max(int P) {
-    (void)P;
-    return 512 << 10;
+    if (P <= 2) return 64 << 10;
+    return 256 << 10;
 }
 
 // NVLS moves about N(1 + 1/P) bytes per GPU and direction plus a local
@@ -1469,12 +1488,12 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
     cail_prof_mark(CAIL_PH_SETUP, ts);
     // A single rank runs the same kernels (they degenerate to a copy).
     if (algo == CAIL_ALGO_ONE_SHOT) {
-        rc = run_oneshot_chunked(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
+        rc = run_oneshot(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
     } else if (algo == CAIL_ALGO_NVLS && cail_dev_nvls_ok(dc, dt, op)) {
         rc = run_nvls(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
     } else if (algo == CAIL_ALGO_CE_TWO_SHOT) {
         rc = run_twoshot(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
-    } else if (twoshot_zero_copy()) {
+    } else if (twoshot_zero_copy(dc)) {
         rc = run_twoshot(dc, src, dst, (size_t)count, esz, (int)op, ec);
     } else {
         rc = run_push(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
@@ -1503,32 +1522,36 @@ int cail_test_device_timeout(int timeout_ms) {
     DevStatus *st_h = nullptr, *st_d = nullptr;
     cudaStream_t s = nullptr;
     int code = -1;
-    // layout: [flags][src 16 KiB][dst 16 KiB][two 16 KiB slots]; the second
-    // "peer" slot and the peer flag array are local memory
-    const size_t part = 16 << 10;
-    if (cudaMalloc(&ws, kFlagBytes + 4 * part) == cudaSuccess &&
-        cudaMemset(ws, 0, kFlagBytes + 4 * part) == cudaSuccess &&
+    // layout: [flags of rank 0][flags of rank 1][src 16 KiB][dst 16 KiB]
+    // [one-shot area of rank 0][of rank 1]; only rank 0's CTA runs, so rank 1
+    // never raises its flag
+    const size_t part = 16 << 10, piece = 16 << 10;
+    const size_t area = (size_t)cail::kOsSlots * 1 * 2 * piece;
+    const size_t total = 2 * kFlagBytes + 2 * part + 2 * area;
+    if (cudaMalloc(&ws, total) == cudaSuccess && cudaMemset(ws, 0, total) == cudaSuccess &&
         cudaHostAlloc((void **)&st_h, sizeof(DevStatus), cudaHostAllocMapped) == cudaSuccess &&
         cudaHostGetDevicePointer((void **)&st_d, st_h, 0) == cudaSuccess &&
         cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess) {
         memset(st_h, 0, sizeof(DevStatus));
         cail::OneShotArgs a;
         memset(&a, 0, sizeof(a));
-        a.count = 1024;
-        a.src = ws + kFlagBytes;
-        a.dst = ws + kFlagBytes + part;
-        a.slot_out[0] = ws + kFlagBytes + 2 * part;
-        a.slot_out[1] = ws + kFlagBytes + 3 * part;
-        a.slot_in = ws + kFlagBytes + 2 * part;
-        a.slot_bytes = part;
-        a.peer_flags[0] = a.peer_flags[1] = (uint32_t *)ws;
-        a.my_flags = (uint32_t *)ws;
+        a.flags[0] = (uint32_t *)ws;
+        a.flags[1] = (uint32_t *)(ws + kFlagBytes);
+        a.src[0] = ws + 2 * kFlagBytes;
+        a.dst[0] = ws + 2 * kFlagBytes + part;
+        a.slots[0] = ws + 2 * kFlagBytes + 2 * part;
+        a.slots[1] = ws + 2 * kFlagBytes + 2 * part + area;
+        a.rounds_done[0] = (uint32_t *)ws + cail::kOsRoundsBase;
+        a.bytes = part;
+        a.piece = piece;
+        a.area = area;
         a.P = 2;
-        a.rank = 0;
-        a.epoch = 1;
+        a.rank0 = 0;
+        a.G = 1;
+        a.vec = 1;
         a.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
         a.status = st_d;
-        if (cail::launch_oneshot(CAIL_SUM, CAIL_EC_F32, a, 1, 128, s) == cudaSuccess &&
+        if (cail::launch_oneshot(CAIL_SUM, CAIL_EC_F32, a, 1, false, s) == cudaSuccess &&
             cudaStreamSynchronize(s) == cudaSuccess)
             code = st_h->code;
     }

@@ -104,108 +104,133 @@ __device__ void report_check(DevStatus *st, int rank, int check) {
 }
 
 // ---------------------------------------------------------------- one-shot
-// Pushes bytes [lo, hi) of src (any alignment) into P destinations (16-byte
-// aligned slots), 16 bytes at a time where src allows it.
-template <typename T>
-__device__ __forceinline__ void block_push(char *const *dst, int P, const char *src, size_t lo, size_t hi) {
-    if (((uintptr_t)src & 15) == 0) {
-        for (size_t i = lo / 16 + threadIdx.x; i < hi / 16; i += blockDim.x) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(src + i * 16);
-#pragma unroll
-            for (int q = 0; q < kMaxRanks; ++q)
-                if (q < P) st_v4(dst[q] + i * 16, v);
-        }
-        for (size_t e = (hi / 16) * 16 / sizeof(T) + threadIdx.x; e < hi / sizeof(T); e += blockDim.x) {
-            const T v = reinterpret_cast<const T *>(src)[e];
-            for (int q = 0; q < P; ++q) reinterpret_cast<T *>(dst[q])[e] = v;
-        }
-    } else {
-        for (size_t e = lo / sizeof(T) + threadIdx.x; e < hi / sizeof(T); e += blockDim.x) {
-            const T v = reinterpret_cast<const T *>(src)[e];
-            for (int q = 0; q < P; ++q) reinterpret_cast<T *>(dst[q])[e] = v;
-        }
-    }
+__device__ __forceinline__ void push_signal_os(const OneShotArgs &a, int me, int b, uint32_t e) {
+    const int t = threadIdx.x;
+    if (t < a.P && t != me) st_release_sys(a.flags[t] + kOsFlagBase + me * kMaxBlocks + b, e);
 }
 
 // CAIL_DEVICE_CHECKS for the one-shot kernel: 0 when the arguments are
 // consistent, else the number of the failed check.
 template <typename T>
 __device__ int oneshot_check(const OneShotArgs &a) {
-    if (a.P < 1 || a.P > kMaxRanks || a.rank < 0 || a.rank >= a.P) return 1;
-    if (gridDim.x > (unsigned)kMaxBlocks) return 2;
-    if (a.count > a.slot_bytes / sizeof(T)) return 3;
-    if (a.slot_bytes % 16 || ((uintptr_t)a.slot_in & 15)) return 4;
+    if (a.P < 2 || a.P > kMaxRanks) return 1;
+    if (a.G < 1 || a.G > kMaxBlocks || gridDim.x % (unsigned)a.G != 0 || a.rank0 < 0 ||
+        a.rank0 + (int)(gridDim.x / (unsigned)a.G) > a.P)
+        return 2;
+    if (a.piece == 0 || a.piece % 16) return 3;
+    if ((size_t)kOsSlots * a.G * a.P * a.piece > a.area) return 4;
+    if (a.bytes % sizeof(T)) return 5;
     for (int q = 0; q < a.P; ++q)
-        if (!a.slot_out[q] || ((uintptr_t)a.slot_out[q] & 15) || !a.peer_flags[q]) return 5;
-    if (!a.src || !a.dst || !a.my_flags) return 6;
+        if (!a.slots[q] || ((uintptr_t)a.slots[q] & 15) || !a.flags[q]) return 7;
+    for (int r = a.rank0; r < a.rank0 + (int)(gridDim.x / (unsigned)a.G); ++r) {
+        if (!a.src[r] || !a.dst[r] || !a.rounds_done[r]) return 8;
+        if (a.vec && ((((uintptr_t)a.src[r]) | ((uintptr_t)a.dst[r])) & 15)) return 8;
+        if (((uintptr_t)a.src[r] | (uintptr_t)a.dst[r]) % sizeof(T)) return 8;
+    }
     return 0;
 }
 
-template <int OP, typename T>
-__global__ void __launch_bounds__(512) oneshot_kernel(OneShotArgs a) {
+// n bytes of src into the same slot of every peer's area (not this rank's):
+// each vector is loaded once and stored P - 1 times.
+template <typename T, bool VEC>
+__device__ __forceinline__ void push_to_peers(const OneShotArgs &a, int me, size_t slot, const char *src, size_t n) {
+    size_t done = 0;
+    if constexpr (VEC) {
+        const size_t nv = n / 16;
+        for (size_t i = threadIdx.x; i < nv; i += blockDim.x) {
+            const uint4 v = ld_v4(src + i * 16);
+#pragma unroll
+            for (int q = 0; q < kMaxRanks; ++q)
+                if (q < a.P && q != me) st_v4(a.slots[q] + slot + i * 16, v);
+        }
+        done = nv * 16;
+    }
+    for (size_t e = done / sizeof(T) + threadIdx.x; e < n / sizeof(T); e += blockDim.x) {
+        const T v = reinterpret_cast<const T *>(src)[e];
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+            if (q < a.P && q != me) reinterpret_cast<T *>(a.slots[q] + slot)[e] = v;
+    }
+}
+
+template <int OP, typename T, bool VEC>
+__global__ void __launch_bounds__(512, 2) oneshot_kernel(OneShotArgs a) {
     __shared__ int s_fail;
     if (a.checks) {
         const int bad = oneshot_check<T>(a);
         if (bad) {
-            report_check(a.status, a.rank, bad);
+            report_check(a.status, a.rank0, bad);
             return;
         }
     }
-    const size_t bytes = a.count * sizeof(T);
-    const size_t n16 = (bytes + 15) / 16;
-    const size_t per = (n16 + gridDim.x - 1) / gridDim.x;
-    const size_t lo = min((size_t)blockIdx.x * per, n16) * 16;
-    const size_t hi = min(min((size_t)(blockIdx.x + 1) * per, n16) * 16, bytes);
+    const int me = a.rank0 + (int)(blockIdx.x / (unsigned)a.G);
+    const int b = (int)(blockIdx.x % (unsigned)a.G);
+    const int P = a.P;
+    const char *src = a.src[me];
+    char *dst = a.dst[me];
     if (threadIdx.x == 0) s_fail = 0;
-
-    // 1. push this block's share of the input into every rank's slot
-    if (hi > lo) block_push<T>(a.slot_out, a.P, a.src, lo, hi);
+    const uint32_t base = a.rounds_done[me][b];  // read by every thread before thread 0 updates it
     __syncthreads();
-
-    // 2. signal every peer (after the block barrier, each release orders the
-    //    block's stores before the flag), 3. wait for every peer's signal
-    const int t = threadIdx.x;
-    if (t < a.P && t != a.rank)
-        st_release_sys(a.peer_flags[t] + a.rank * kMaxBlocks + blockIdx.x, a.epoch);
-    if (t < a.P && t != a.rank) {
-        uint32_t seen = 0;
-        unsigned long long deadline = globaltimer() + a.timeout_ns;
-        if (!wait_flag(a.my_flags + t * kMaxBlocks + blockIdx.x, a.epoch, deadline, &seen)) {
-            report(a.status, a.rank, t, blockIdx.x, a.epoch, seen);
-            s_fail = 1;
+    auto off = [&](uint32_t k) { return ((size_t)k * a.G + b) * a.piece; };
+    auto slot_of = [&](uint32_t e, int q) { return (((size_t)(e % kOsSlots) * a.G + b) * P + q) * a.piece; };
+    auto push = [&](uint32_t k) {
+        const uint32_t e = base + k + 1;
+        const size_t o = off(k);
+        push_to_peers<T, VEC>(a, me, slot_of(e, me), src + o, min(a.piece, a.bytes - o));
+        __syncthreads();
+        push_signal_os(a, me, b, e);
+    };
+    if (off(0) < a.bytes) push(0);
+    uint32_t k = 0;
+    for (; off(k) < a.bytes; ++k) {
+        const uint32_t e = base + k + 1;
+        const size_t o = off(k);
+        const size_t n = min(a.piece, a.bytes - o);
+        // wait for every peer's piece of round k
+        if (threadIdx.x < P && threadIdx.x != me) {
+            uint32_t seen = 0;
+            const unsigned long long deadline = globaltimer() + a.timeout_ns;
+            if (!wait_flag(a.flags[me] + kOsFlagBase + threadIdx.x * kMaxBlocks + b, e, deadline, &seen)) {
+                report(a.status, me, threadIdx.x, b, e, seen);
+                s_fail = 1;
+            }
+        }
+        __syncthreads();
+        if (s_fail) return;
+        if (off(k + 1) < a.bytes) push(k + 1);  // look ahead (three rotating slots)
+        // fold round k in rank order
+        const char *own_in = src + o;
+        char *out = dst + o;
+        const char *area0 = a.slots[me] + slot_of(e, 0);
+        size_t done = 0;
+        if constexpr (VEC) {
+            const size_t nv = n / 16;
+            for (size_t i = threadIdx.x; i < nv; i += blockDim.x) {
+                uint4 v[kMaxRanks];
+#pragma unroll
+                for (int q = 0; q < kMaxRanks; ++q)
+                    if (q < P) v[q] = ld_v4((q == me ? own_in : area0 + q * a.piece) + i * 16);
+                uint4 acc = v[0];
+#pragma unroll
+                for (int q = 1; q < kMaxRanks; ++q)
+                    if (q < P) acc = vop<OP, T>(acc, v[q]);
+                st_v4(out + i * 16, acc);
+            }
+            done = nv * 16;
+        }
+        for (size_t el = done / sizeof(T) + threadIdx.x; el < n / sizeof(T); el += blockDim.x) {
+            T acc = T();
+#pragma unroll
+            for (int q = 0; q < kMaxRanks; ++q)
+                if (q < P) {
+                    const T x = reinterpret_cast<const T *>(q == me ? own_in : area0 + q * a.piece)[el];
+                    acc = q == 0 ? x : apply<OP, T>(acc, x);
+                }
+            reinterpret_cast<T *>(out)[el] = acc;
         }
     }
     __syncthreads();
-    if (s_fail) return;
-
-    // 4. fold the P local slots in rank order
-    const size_t vlo = lo / 16, vhi = hi / 16;
-    const bool dst_vec = ((uintptr_t)a.dst & 15) == 0;
-    for (size_t i = vlo + threadIdx.x; i < vhi; i += blockDim.x) {
-        uint4 v[kMaxRanks];
-#pragma unroll
-        for (int q = 0; q < kMaxRanks; ++q)
-            if (q < a.P) v[q] = ld_v4(a.slot_in + (size_t)q * a.slot_bytes + i * 16);
-        uint4 acc = v[0];
-#pragma unroll
-        for (int q = 1; q < kMaxRanks; ++q)
-            if (q < a.P) acc = vop<OP, T>(acc, v[q]);
-        if (dst_vec) {
-            st_v4(a.dst + i * 16, acc);
-        } else {
-            const T *pa = reinterpret_cast<const T *>(&acc);
-#pragma unroll
-            for (int k = 0; k < (int)(16 / sizeof(T)); ++k)
-                reinterpret_cast<T *>(a.dst + i * 16)[k] = pa[k];
-        }
-    }
-    // ragged end (last block only)
-    for (size_t e = vhi * 16 / sizeof(T) + threadIdx.x; e < hi / sizeof(T); e += blockDim.x) {
-        T acc = reinterpret_cast<const T *>(a.slot_in)[e];
-        for (int q = 1; q < a.P; ++q)
-            acc = apply<OP, T>(acc, reinterpret_cast<const T *>(a.slot_in + (size_t)q * a.slot_bytes)[e]);
-        reinterpret_cast<T *>(a.dst)[e] = acc;
-    }
+    if (threadIdx.x == 0) a.rounds_done[me][b] = base + k;
 }
 
 // ---------------------------------------------------------------- two-shot
@@ -761,10 +786,17 @@ namespace {
 
 struct LaunchOneShot {
     const OneShotArgs &a;
-    int b, t;
+    int ranks;
+    bool coop;
     cudaStream_t s;
+    cudaError_t err = cudaSuccess;
     template <int OP, int EC> void operator()() {
-        oneshot_kernel<OP, typename EcType<EC>::T><<<b, t, 0, s>>>(a);
+        using T = typename EcType<EC>::T;
+        void *k = a.vec ? (void *)oneshot_kernel<OP, T, true> : (void *)oneshot_kernel<OP, T, false>;
+        const dim3 grid((unsigned)(a.G * ranks)), block(512);
+        void *args[] = {(void *)&a};
+        err = coop ? cudaLaunchCooperativeKernel(k, grid, block, args, 0, s)
+                   : cudaLaunchKernel(k, grid, block, args, 0, s);
     }
 };
 
@@ -849,10 +881,10 @@ struct LaunchReduceLocal {
 
 }  // namespace
 
-cudaError_t launch_oneshot(int op, int ec, const OneShotArgs &a, int blocks, int threads,
-                           cudaStream_t s) {
-    LaunchOneShot l{a, blocks, threads, s};
+cudaError_t launch_oneshot(int op, int ec, const OneShotArgs &a, int ranks, bool cooperative, cudaStream_t s) {
+    LaunchOneShot l{a, ranks, cooperative, s};
     if (!dispatch_op_class(op, ec, l)) return cudaErrorInvalidValue;
+    if (l.err != cudaSuccess) return l.err;
     return cudaGetLastError();
 }
 

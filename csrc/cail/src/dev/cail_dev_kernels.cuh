@@ -22,22 +22,34 @@ struct DevStatus {
     unsigned int seen;
 };
 
-// One-shot (push): every rank writes its input into slot `rank` of every
-// rank's scratch (posted NVLink stores), signals each peer with a release
-// flag per CTA, waits for the P-1 flags addressed to it, then folds its P
-// local slots in rank order into its output.  Scratch is double-buffered
-// by epoch parity, so no trailing barrier is needed.
+// One-shot (push): every rank pushes its whole input, piece by piece, into
+// its slot of every other rank's one-shot area (NVLink stores), and every
+// rank folds the P copies of each piece in rank order (its own piece straight
+// from its input) into its output.  CTA b of every rank handles, in round k,
+// the piece at byte offset (k * G + b) * piece:
+//   wait until every peer raised OS[q][b] >= epoch (its piece of round k is
+//   in this rank's area), push the piece of round k + 1 and raise
+//   OS[rank][b] = epoch + 1 on every peer, then fold round k.
+// Round k + 1 goes out before round k is folded, so slots rotate through
+// three: the slot of round k + 1 was last used by round k - 2, which every
+// peer folded before it raised the flag of round k that this CTA has just
+// received.  The rotation must advance by exactly one per round of a CTA,
+// across calls too, so each CTA keeps its own completed-round count in
+// `rounds_done` (this GPU's memory; the same on every rank because every rank
+// runs the same rounds): round k of a call has epoch rounds_done[b] + k + 1.
+// A single round per CTA (small messages) costs one flag exchange.
+constexpr int kOsSlots = 3;
 struct OneShotArgs {
-    const char *src;                 // this rank's input (user buffer)
-    char *dst;                       // this rank's output (user buffer)
-    size_t count;                    // elements (count * size <= slot bytes)
-    char *slot_out[kMaxRanks];       // slot `rank` of each rank's scratch, this parity (peer mappings)
-    const char *slot_in;             // slot 0 of this rank's scratch, this parity
-    size_t slot_bytes;               // distance between slots
-    uint32_t *peer_flags[kMaxRanks]; // each rank's arrival flag array (peer mappings)
-    uint32_t *my_flags;              // this rank's arrival flag array
-    int P, rank;
-    uint32_t epoch;
+    const char *src[kMaxRanks];      // input of each rank this launch runs (production: [rank])
+    char *dst[kMaxRanks];            // output of each rank this launch runs
+    char *slots[kMaxRanks];          // one-shot area of every rank (peer mappings)
+    uint32_t *flags[kMaxRanks];      // flag array of every rank (peer mappings)
+    uint32_t *rounds_done[kMaxRanks];// per-CTA completed rounds of each rank this launch runs
+    size_t bytes;                    // message bytes
+    size_t piece;                    // bytes per CTA and round (a multiple of 16)
+    size_t area;                     // bytes of each one-shot area
+    int P, rank0, G;
+    int vec;                         // every user buffer is 16-byte aligned
     unsigned long long timeout_ns;
     DevStatus *status;
     int checks;                      // validate the arguments first (CAIL_DEVICE_CHECKS)
@@ -88,8 +100,12 @@ struct TwoShotArgs {
 // reports DevStatus code 2 with the check's number and returns before it
 // touches memory or waits on a flag; every CTA sees the same arguments, so
 // all of them return.
-constexpr int kRsFlagBase = kFlagWords;      // word offsets in the flag array
+constexpr int kOsFlagBase = 0;               // word offsets in the flag array
+constexpr int kRsFlagBase = kFlagWords;
 constexpr int kAgFlagBase = 2 * kFlagWords;
+constexpr int kNvlsStepsBase = 3 * kFlagWords;      // NVLS per-CTA steps (kMaxBlocks words)
+constexpr int kOsRoundsBase = 3 * kFlagWords + kMaxBlocks;  // one-shot per-CTA rounds (kMaxBlocks words)
+constexpr int kFlagAreaWords = 3 * kFlagWords + 2 * kMaxBlocks;
 struct PushArgs {
     const char *src[kMaxRanks];      // input of each rank this launch runs (production: [rank])
     char *dst[kMaxRanks];            // output of each rank this launch runs
@@ -160,8 +176,9 @@ struct FoldArgs {
 
 // Launchers: return cudaSuccess or the launch error.  ec is a
 // cail_elem_class_t, op a cail_op_t.
-cudaError_t launch_oneshot(int op, int ec, const OneShotArgs &a, int blocks, int threads,
-                           cudaStream_t s);
+// One-shot: a.G * ranks CTAs of 512 threads (ranks = 1 in production;
+// cooperative for the one-GPU emulation of several ranks).
+cudaError_t launch_oneshot(int op, int ec, const OneShotArgs &a, int ranks, bool cooperative, cudaStream_t s);
 cudaError_t launch_twoshot(int op, int ec, const TwoShotArgs &a, int blocks, int threads,
                            cudaStream_t s);
 cudaError_t launch_nvls(int op, int ec, const NvlsArgs &a, int blocks, cudaStream_t s);

@@ -55,33 +55,45 @@ struct Bufs {
     }
 };
 
-// Emulated push two-shot: P workspaces, each [flags | RS area | AG area].
-struct PushEmu {
+// Emulated ranks' workspaces: rank q's is [flag area | one-shot area | RS area
+// | AG area], all on this GPU.
+struct Emu {
     Bufs b;
     char *ws[cail::kMaxRanks] = {};
-    size_t area = 0;
+    size_t os_area = 0, area = 0;
     uint32_t epoch = 0;
     cail::DevStatus *st = nullptr;
+    static constexpr size_t kFlags = 64 << 10;
     bool init(int P, int G, size_t piece) {
+        os_area = ((size_t)cail::kOsSlots * G * P * piece + 255) / 256 * 256;
         area = ((size_t)2 * G * P * piece + 255) / 256 * 256;
-        const size_t flags = (size_t)3 * cail::kFlagWords * sizeof(uint32_t);
         for (int q = 0; q < P; ++q)
-            if (!(ws[q] = b.get(flags + 2 * area))) return false;
+            if (!(ws[q] = b.get(kFlags + os_area + 2 * area))) return false;
         st = (cail::DevStatus *)b.get(sizeof(cail::DevStatus));
         return st != nullptr;
     }
-    // fills the per-call part of a (epochs advance by the rounds of the call)
+    // fills the per-call part of a push (epochs advance by the rounds of the call)
     void args(cail::PushArgs &a, int P, unsigned long long timeout_ns) {
-        const size_t flags = (size_t)3 * cail::kFlagWords * sizeof(uint32_t);
         for (int q = 0; q < P; ++q) {
             a.flags[q] = (uint32_t *)ws[q];
-            a.rs[q] = ws[q] + flags;
-            a.ag[q] = ws[q] + flags + area;
+            a.rs[q] = ws[q] + kFlags + os_area;
+            a.ag[q] = ws[q] + kFlags + os_area + area;
         }
         a.rank0 = 0;
         a.area = area;
         a.epoch0 = epoch + 1;
         epoch += (uint32_t)a.rounds;
+        a.timeout_ns = timeout_ns;
+        a.status = st;
+    }
+    void args(cail::OneShotArgs &a, int P, unsigned long long timeout_ns) {
+        for (int q = 0; q < P; ++q) {
+            a.flags[q] = (uint32_t *)ws[q];
+            a.slots[q] = ws[q] + kFlags;
+            a.rounds_done[q] = (uint32_t *)ws[q] + cail::kOsRoundsBase;
+        }
+        a.rank0 = 0;
+        a.area = os_area;
         a.timeout_ns = timeout_ns;
         a.status = st;
     }
@@ -132,7 +144,7 @@ extern "C" int cail_emulate_push(int P, const void *const *srcs, void *const *ds
     bool vec = true;
     for (int q = 0; q < P; ++q)
         if ((((uintptr_t)srcs[q]) | ((uintptr_t)dsts[q])) & 15) vec = false;
-    PushEmu emu;
+    Emu emu;
     if (!emu.init(P, G, piece)) return -1;
     cudaStream_t s = nullptr;
     if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return -1;
@@ -162,7 +174,59 @@ extern "C" int cail_emulate_push(int P, const void *const *srcs, void *const *ds
     return rc;
 }
 
-// kernel: 0 = one_shot (peers' flags set in advance, so it never waits),
+// The one-shot allreduce of P emulated ranks, as cail_emulate_push (same
+// arguments; `piece` 0: 16 KiB; options bit 0: argument checks).
+extern "C" int cail_emulate_oneshot(int P, const void *const *srcs, void *const *dsts, size_t count, int ec,
+                                    int op, int G, size_t piece, int calls, int options) {
+    if (P < 2 || P > cail::kMaxRanks || calls < 1 || !srcs || !dsts) return -1;
+    static const int esz_of[CAIL_EC_NUM] = {1, 1, 2, 2, 4, 4, 8, 8, 4, 8};
+    if (ec < 0 || ec >= CAIL_EC_NUM) return -1;
+    const size_t esz = (size_t)esz_of[ec];
+    if (piece == 0) piece = 16 << 10;
+    if (piece % 16) return -1;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int gmax = cail::push_max_ctas(P, sms);
+    if (G <= 0 || G > gmax) G = gmax;
+    bool vec = true;
+    for (int q = 0; q < P; ++q)
+        if ((((uintptr_t)srcs[q]) | ((uintptr_t)dsts[q])) & 15) vec = false;
+    Emu emu;
+    if (!emu.init(P, G, piece)) return -1;
+    cudaStream_t s = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return -1;
+    int rc = 0;
+    for (int c = 0; c < calls && rc == 0; ++c) {
+        cail::OneShotArgs a;
+        memset(&a, 0, sizeof(a));
+        a.bytes = count * esz;
+        a.piece = piece;
+        a.P = P;
+        a.G = G;
+        a.vec = vec ? 1 : 0;
+        for (int q = 0; q < P; ++q) {
+            a.src[q] = (const char *)srcs[q];
+            a.dst[q] = (char *)dsts[q];
+        }
+        emu.args(a, P, 2000000000ull);
+        a.checks = options & 1;
+        if (cail::launch_oneshot(op, ec, a, P, true, s) != cudaSuccess) rc = -1;
+    }
+    cail::DevStatus h;
+    memset(&h, 0, sizeof(h));
+    if (cudaStreamSynchronize(s) != cudaSuccess ||
+        cudaMemcpy(&h, emu.st, sizeof(h), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = -1;
+    else if (rc == 0 && h.code != 0)
+        rc = h.code;
+    cudaStreamDestroy(s);
+    cudaGetLastError();
+    return rc;
+}
+
+// kernel: 0 = one_shot of P emulated ranks (one cooperative launch; the time
+// is per call of all P ranks),
 // 1 = zero-copy two_shot (reads P inputs, writes P outputs), 2 = fold (P
 // sources), 3 = bulk (TMA) copy, 4 = push two_shot of P emulated ranks (one
 // cooperative launch; the time is per call of all P ranks), 5 = copy kernel,
@@ -186,37 +250,38 @@ extern "C" int cail_bench_kernel_local(int kernel, int P, size_t bytes, int iter
     cail::DevStatus *st = (cail::DevStatus *)b.get(sizeof(cail::DevStatus));
     int rc = 0;
     if (kernel == 0) {
-        const size_t slot = bytes;
-        char *src = b.get(bytes), *dst = b.get(bytes);
-        uint32_t *flags = (uint32_t *)b.get(cail::kFlagWords * 4);
-        std::vector<char *> area(P);
-        for (int q = 0; q < P; ++q) area[q] = b.get(slot * P);
-        if (!src || !dst || !flags || !st) { rc = -1; goto out; }
-        // every peer has already arrived for all epochs used below
-        cudaMemset(flags, 0x7f, cail::kFlagWords * 4);
-        cail::OneShotArgs a;
-        memset(&a, 0, sizeof(a));
-        a.src = src;
-        a.dst = dst;
-        a.count = count;
+        if (P < 2) { rc = -1; goto out; }
+        std::vector<char *> src(P), dst(P);
         for (int q = 0; q < P; ++q) {
-            a.slot_out[q] = area[q];  // this rank is rank 0: slot 0 of each peer's area
-            a.peer_flags[q] = flags;
+            src[q] = b.get(bytes);
+            dst[q] = b.get(bytes);
+            if (!src[q] || !dst[q]) { rc = -1; goto out; }
         }
-        a.slot_in = area[0];
-        a.slot_bytes = slot;
-        a.my_flags = flags;
-        a.P = P;
-        a.rank = 0;
-        a.epoch = 1;
-        a.timeout_ns = 1000000000ull;
-        a.status = st;
-        size_t vec = (bytes + 15) / 16;
-        size_t want = (vec + 1023) / 1024;
-        int blocks = (int)(want < 1 ? 1 : (want > (size_t)cail::kMaxBlocks ? cail::kMaxBlocks : want));
-        cail::launch_oneshot(CAIL_SUM, CAIL_EC_F32, a, blocks, 512, s);  // warm-up
+        const int G = cail::push_max_ctas(P, sms);
+        size_t piece = (bytes + G - 1) / G;
+        piece = (piece + 8191) / 8192 * 8192;
+        if (piece > (16 << 10)) piece = 16 << 10;
+        const int g = (int)((bytes + piece - 1) / piece < (size_t)G ? (bytes + piece - 1) / piece : (size_t)G);
+        Emu emu;
+        if (!emu.init(P, G, piece)) { rc = -1; goto out; }
+        auto launch = [&]() {
+            cail::OneShotArgs a;
+            memset(&a, 0, sizeof(a));
+            a.bytes = bytes;
+            a.piece = piece;
+            a.P = P;
+            a.G = g;
+            a.vec = 1;
+            for (int q = 0; q < P; ++q) {
+                a.src[q] = src[q];
+                a.dst[q] = dst[q];
+            }
+            emu.args(a, P, 2000000000ull);
+            return cail::launch_oneshot(CAIL_SUM, CAIL_EC_F32, a, P, true, s);
+        };
+        if (launch() != cudaSuccess) { rc = -1; goto out; }
         cudaEventRecord(e0, s);
-        for (int i = 0; i < iters; ++i) cail::launch_oneshot(CAIL_SUM, CAIL_EC_F32, a, blocks, 512, s);
+        for (int i = 0; i < iters; ++i) launch();
         cudaEventRecord(e1, s);
     } else if (kernel == 3 || kernel == 5) {
         char *src = b.get(bytes + 16), *dst = b.get(bytes + 16);
@@ -269,7 +334,7 @@ extern "C" int cail_bench_kernel_local(int kernel, int P, size_t bytes, int iter
         }
         const int G = cail::push_max_ctas(P, sms);
         const size_t piece = 32 << 10;
-        PushEmu emu;
+        Emu emu;
         if (!emu.init(P, G, piece)) { rc = -1; goto out; }
         auto launch = [&]() {
             cail::PushArgs a;

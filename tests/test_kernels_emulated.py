@@ -1,7 +1,8 @@
 """One-GPU tests of cail's multi-rank kernels with the ranks emulated.
 
-The push two-shot allreduce of P ranks runs as one cooperative launch on one
-GPU (libcail_kbench's cail_emulate_push): every emulated rank has its own
+The push two-shot and the one-shot allreduce of P ranks each run as one
+cooperative launch on one GPU (libcail_kbench's cail_emulate_push and
+cail_emulate_oneshot): every emulated rank has its own
 input, output, workspace and flag array, and the ranks' CTAs synchronise
 through the same release/acquire flags as across GPUs.  Oracle: the
 rank-order fold acc = x_0; acc = op(acc, x_1); ... computed on the CPU with
@@ -33,9 +34,9 @@ def _lib():
     ctypes.CDLL(os.path.join(LIB, "libcail.so"), mode=ctypes.RTLD_GLOBAL)
     k = ctypes.CDLL(os.path.join(LIB, "libcail_kbench.so"))
     vp = ctypes.c_void_p
-    k.cail_emulate_push.argtypes = [ctypes.c_int, ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.c_size_t,
-                                    ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_int,
-                                    ctypes.c_int]
+    for fn in (k.cail_emulate_push, k.cail_emulate_oneshot):
+        fn.argtypes = [ctypes.c_int, ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.c_size_t,
+                       ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_int, ctypes.c_int]
     k.cail_bench_kernel_local.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_int,
                                           ctypes.POINTER(ctypes.c_float)]
     return k
@@ -81,9 +82,11 @@ def _signed_view(dt):
     return {np.uint16: np.int16, np.uint32: np.int32, np.uint64: np.int64}.get(dt, dt)
 
 
-def _run(k, P, xs, op_i, ec, offset=0, in_place=False, G=0, piece=0, calls=2, options=1, expect_rc=0):
+def _run(k, P, xs, op_i, ec, offset=0, in_place=False, G=0, piece=0, calls=2, options=1, expect_rc=0,
+         kind="push"):
     """Uploads xs (one array per rank) at `offset` elements into fresh device
-    buffers, runs the emulated push two-shot and returns the P outputs."""
+    buffers, runs the emulated kernel (kind: push or oneshot) and returns the
+    P outputs."""
     import torch
 
     dt = xs[0].dtype
@@ -106,26 +109,32 @@ def _run(k, P, xs, op_i, ec, offset=0, in_place=False, G=0, piece=0, calls=2, op
     vp = ctypes.c_void_p
     sa = (vp * P)(*[s.data_ptr() for s in srcs])
     da = (vp * P)(*[d.data_ptr() for d in dsts])
-    rc = k.cail_emulate_push(P, sa, da, n, ec, op_i, G, piece, 1 if in_place else calls, options)
+    fn = k.cail_emulate_push if kind == "push" else k.cail_emulate_oneshot
+    rc = fn(P, sa, da, n, ec, op_i, G, piece, 1 if in_place else calls, options)
     torch.cuda.synchronize()
     assert rc == expect_rc, f"cail_emulate_push returned {rc}"
     return [d.cpu().numpy().view(dt) for d in dsts]
 
 
+KINDS = ["push", "oneshot"]
+
+
+@pytest.mark.parametrize("kind", KINDS)
 @pytest.mark.parametrize("ec", range(10), ids=[np.dtype(t).name for t in EC])
 @pytest.mark.parametrize("op", OPS)
-def test_push_two_shot_emulated_all_types_bit_exact(ec, op):
+def test_emulated_kernels_all_types_bit_exact(kind, ec, op):
     k = _lib()
     rng = np.random.default_rng(1000 + 10 * ec + OPS.index(op))
     for P, n in ((2, 4099), (3, 100003), (8, 1), (8, 7), (8, 65536 + 3)):
         xs = _inputs(rng, EC[ec], op, P, n)
         want = _fold(xs, op)
-        for r, got in enumerate(_run(k, P, xs, OPS.index(op), ec)):
+        for r, got in enumerate(_run(k, P, xs, OPS.index(op), ec, kind=kind)):
             assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (P, n, r)
 
 
+@pytest.mark.parametrize("kind", KINDS)
 @pytest.mark.parametrize("P", [2, 4, 5, 8])
-def test_push_two_shot_emulated_unaligned_and_in_place(P):
+def test_emulated_kernels_unaligned_and_in_place(kind, P):
     """Buffers one element off a 16-byte boundary take the element-wise path;
     in-place calls (input = output) must give the same result."""
     k = _lib()
@@ -133,22 +142,24 @@ def test_push_two_shot_emulated_unaligned_and_in_place(P):
     for ec, n in ((8, 300001), (1, 77777), (9, 4097)):
         xs = _inputs(rng, EC[ec], "sum", P, n)
         want = _fold(xs, "sum")
-        for got in _run(k, P, xs, 0, ec, offset=1):
+        for got in _run(k, P, xs, 0, ec, offset=1, kind=kind):
             assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (P, ec, n, "offset")
-        for got in _run(k, P, xs, 0, ec, in_place=True):
+        for got in _run(k, P, xs, 0, ec, in_place=True, kind=kind):
             assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (P, ec, n, "in place")
 
 
-def test_push_two_shot_emulated_many_rounds():
+@pytest.mark.parametrize("kind", KINDS)
+def test_emulated_kernels_many_rounds(kind):
     """Few CTAs and small pieces: every CTA runs many rounds, so its slots
-    alternate between the two parities within one call and across calls."""
+    rotate (two parities for the push two-shot, three slots for the
+    one-shot) within one call and across calls."""
     k = _lib()
     rng = np.random.default_rng(5)
     for P, G, piece in ((2, 1, 256), (4, 3, 512), (8, 2, 1024)):
         xs = _inputs(rng, np.float32, "sum", P, 250007)
         want = _fold(xs, "sum")
-        for got in _run(k, P, xs, 0, 8, G=G, piece=piece, calls=3):
-            assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (P, G, piece)
+        for got in _run(k, P, xs, 0, 8, G=G, piece=piece, calls=3, kind=kind):
+            assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (kind, P, G, piece)
 
 
 def test_device_checks_catch_an_inconsistent_argument():

@@ -43,11 +43,15 @@ def query(cases, env=None, stderr=None):
     return json.loads(r.stdout.strip().splitlines()[-1])
 
 
-def test_default_crossover_is_512_kib_and_two_shot_above():
-    cases = [(8, 32 * KIB, "MPI_FLOAT", "MPI_SUM"), (8, 512 * KIB, "MPI_FLOAT", "MPI_SUM"),
-             (8, 512 * KIB + 4, "MPI_FLOAT", "MPI_SUM"), (8, GIB, "MPI_FLOAT", "MPI_SUM"),
-             (2, GIB, "MPI_DOUBLE", "MPI_MAX"), (4, 16 * MIB, "MPI_INT", "MPI_PROD")]
-    assert query(cases) == ["one_shot", "one_shot", "two_shot", "two_shot", "two_shot", "two_shot"]
+def test_default_crossover_per_rank_count_and_two_shot_above():
+    # measured: one_shot up to 64 KiB at 2 ranks, up to 256 KiB at 4 and 8
+    cases = [(8, 32 * KIB, "MPI_FLOAT", "MPI_SUM"), (8, 256 * KIB, "MPI_FLOAT", "MPI_SUM"),
+             (8, 256 * KIB + 4, "MPI_FLOAT", "MPI_SUM"), (8, GIB, "MPI_FLOAT", "MPI_SUM"),
+             (2, 64 * KIB, "MPI_FLOAT", "MPI_SUM"), (2, 64 * KIB + 4, "MPI_FLOAT", "MPI_SUM"),
+             (2, GIB, "MPI_DOUBLE", "MPI_MAX"), (4, 256 * KIB, "MPI_INT", "MPI_PROD"),
+             (4, 16 * MIB, "MPI_INT", "MPI_PROD")]
+    assert query(cases) == ["one_shot", "one_shot", "two_shot", "two_shot", "one_shot", "two_shot", "two_shot",
+                            "one_shot", "two_shot"]
 
 
 def test_unsupported_type_or_op_has_no_nvlink_algorithm():
@@ -97,7 +101,7 @@ def test_tune_file_sets_crossovers_per_rank_count(tmp_path):
              (8, 64 * MIB, "MPI_FLOAT", "MPI_PROD"),
              (4, MIB, "MPI_FLOAT", "MPI_SUM"), (4, MIB + 4, "MPI_FLOAT", "MPI_SUM"),
              (4, 128 * MIB, "MPI_FLOAT", "MPI_SUM"),
-             (2, 512 * KIB, "MPI_FLOAT", "MPI_SUM"), (2, MIB, "MPI_FLOAT", "MPI_SUM")]
+             (2, 64 * KIB, "MPI_FLOAT", "MPI_SUM"), (2, MIB, "MPI_FLOAT", "MPI_SUM")]
     err = []
     got = query(cases, {"CAIL_TUNE_FILE": str(f)}, stderr=err)
     assert got == ["one_shot", "two_shot", "nvls", "two_shot", "two_shot",
@@ -156,5 +160,5 @@ def test_info_tool_prints_the_policy_table(tmp_path):
     row2 = next(l for l in lines if l.startswith("2 ")).split()
     row8 = next(l for l in lines if l.startswith("8 ")).split()
     # columns: 32K 256K 512K 1M 16M 256M 1G
-    assert row2[1:] == ["one_shot", "one_shot", "one_shot", "two_shot", "two_shot", "two_shot", "two_shot"]
+    assert row2[1:] == ["one_shot", "two_shot", "two_shot", "two_shot", "two_shot", "two_shot", "two_shot"]
     assert row8[1:] == ["one_shot", "one_shot", "two_shot", "two_shot", "two_shot", "nvls", "nvls"]
