@@ -565,7 +565,7 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     ap.location.id = cd;
     ap.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;  // as the multicast object
     size_t g1 = 0, g2 = 0;
-    const size_t want = kNvlsCtrRegion + (size_t)blocks * unit;
+    const size_t want = kNvlsCtrRegion + (size_t)blocks * 2 * unit;  // two staging slots per CTA
     mp.size = want;
     ok = nvls_step(dc, ok, g_drv.multicastGetGranularity(&g1, &mp, CU_MULTICAST_GRANULARITY_MINIMUM),
                    "cuMulticastGetGranularity");
@@ -629,8 +629,8 @@ void nvls_setup(cail_dev_comm *dc, bool all_capable) {
     if (!agree(dc->comm, ok)) { nvls_teardown(dc); return; }
     dc->nvls_blocks = blocks;
     dc->nvls = true;
-    CAIL_DBG("nvls: multicast region of %zu bytes (granularity %zu), %d CTA slots of %zu bytes", size, gran, blocks,
-             unit);
+    CAIL_DBG("nvls: multicast region of %zu bytes (granularity %zu), %d CTAs x 2 slots of %zu bytes", size, gran,
+             blocks, unit);
 }
 
 void ce_teardown(cail_dev_comm *dc) {

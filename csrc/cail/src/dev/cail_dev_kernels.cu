@@ -601,18 +601,83 @@ __device__ int nvls_check(const NvlsArgs &a) {
     if (a.P < 2 || a.P > kMaxRanks || a.rank < 0 || a.rank >= a.P) return 1;
     if (gridDim.x > (unsigned)kMaxBlocks) return 2;
     if (a.unit == 0 || a.unit % 16 || a.unit % MB) return 3;
-    if ((size_t)gridDim.x * a.unit > a.area) return 4;
+    if ((size_t)gridDim.x * 2 * a.unit > a.area) return 4;
     if (((uintptr_t)a.uc | (uintptr_t)a.mc) & 15) return 5;
     if (!a.src || !a.dst || !a.mc_ctr || !a.uc_ctr || !a.steps) return 6;
     if (a.bytes % sizeof(T) || ((uintptr_t)a.src | (uintptr_t)a.dst) % sizeof(T)) return 7;
     return 0;
 }
 
+// Warp roles of the NVLS kernel: the first kNvlsCopyWarps warps copy units
+// into and out of the CTA's two staging slots, the others run the multimem
+// reduction; thread kNvlsLeader (the first reducer) meets the other ranks.
+constexpr int kNvlsCopyWarps = 4;
+constexpr int kNvlsCopiers = kNvlsCopyWarps * 32;
+constexpr int kNvlsReducers = 512 - kNvlsCopiers;
+constexpr int kNvlsLeader = kNvlsCopiers;
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"((uint32_t)__cvta_generic_to_shared(bar)) : "memory");
+}
+// Waits for the phase with the given parity to complete; false when the
+// deadline passed or *fail was raised meanwhile.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned long long deadline,
+                                          volatile int *fail) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(bar);
+    for (;;) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (*fail || globaltimer() > deadline) return false;
+    }
+}
+
+// n bytes with the copier threads (tid in [0, kNvlsCopiers)); 16-byte vectors
+// (four in flight per thread) when both ends are aligned.
+template <typename T>
+__device__ __forceinline__ void copier_copy(char *dst, const char *src, size_t n, int tid) {
+    size_t done = 0;
+    if ((((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
+        constexpr int U = 4;
+        const size_t nv = n / 16;
+        size_t i = tid;
+        for (; i + (U - 1) * kNvlsCopiers < nv; i += U * kNvlsCopiers) {
+            uint4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) v[u] = ld_v4(src + (i + u * kNvlsCopiers) * 16);
+#pragma unroll
+            for (int u = 0; u < U; ++u) st_v4(dst + (i + u * kNvlsCopiers) * 16, v[u]);
+        }
+        for (; i < nv; i += kNvlsCopiers) st_v4(dst + i * 16, ld_v4(src + i * 16));
+        done = nv * 16;
+    }
+    for (size_t e = done / sizeof(T) + tid; e < n / sizeof(T); e += kNvlsCopiers)
+        reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+}
+
+// One CTA per staging pair: copier warps move unit k + 1 in and unit k - 1
+// out while the reducer warps run unit k through the switch, so the local
+// copies overlap the NVLink traffic.  Slot k % 2 holds unit k; the copiers
+// refill it (unit k + 2) only after barrier B of unit k, after which no rank
+// touches it until barrier A of unit k + 2.  Hand-offs inside the CTA go
+// through shared-memory mbarriers: full[s] (all copier threads arrive after
+// a copy-in) and done[s] (the leader arrives after barrier B).
 template <int OP, int EC>
 __global__ void __launch_bounds__(512, 2) nvls_kernel(NvlsArgs a) {
     using T = typename EcType<EC>::T;
     using M = Mm<OP, EC>;
     __shared__ int s_fail;
+    __shared__ __align__(8) uint64_t full[2], done[2];
     if (a.checks) {
         const int bad = nvls_check<T, M::bytes>(a);
         if (bad) {
@@ -622,53 +687,78 @@ __global__ void __launch_bounds__(512, 2) nvls_kernel(NvlsArgs a) {
     }
     const int b = blockIdx.x;
     const int G = gridDim.x;
-    if (threadIdx.x == 0) s_fail = 0;
-    const uint32_t base = a.steps[b];  // read before any thread of this CTA can update it
+    const int tid = threadIdx.x;
+    const uint32_t base = a.steps[b];  // read by every thread before the leader updates it
+    // units of this CTA: b, b + G, ...
+    const size_t units = (a.bytes + a.unit - 1) / a.unit;
+    const uint32_t K = (uint32_t)((units - b + G - 1) / G);
+    if (tid == 0) {
+        s_fail = 0;
+        mbar_init(&full[0], kNvlsCopiers);
+        mbar_init(&full[1], kNvlsCopiers);
+        mbar_init(&done[0], 1);
+        mbar_init(&done[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     __syncthreads();
-    char *slot_uc = a.uc + (size_t)b * a.unit;
-    char *slot_mc = a.mc + (size_t)b * a.unit;
+    volatile int *fail = &s_fail;
+    auto slot_uc = [&](uint32_t k) { return a.uc + ((size_t)b * 2 + (k & 1)) * a.unit; };
+    auto slot_mc = [&](uint32_t k) { return a.mc + ((size_t)b * 2 + (k & 1)) * a.unit; };
+    auto unit_off = [&](uint32_t k) { return ((size_t)k * G + b) * a.unit; };
+    auto unit_len = [&](uint32_t k) { return min(a.unit, a.bytes - unit_off(k)); };
+
+    if (tid < kNvlsCopiers) {
+        for (uint32_t k = 0; k < K + 2; ++k) {
+            if (k >= 2) {  // copy-out of unit k - 2 (needs its barrier B)
+                const uint32_t j = k - 2;
+                if (!mbar_wait(&done[j & 1], (j >> 1) & 1, globaltimer() + 4 * a.timeout_ns, fail)) return;
+                fence_proxy_alias();
+                copier_copy<T>(a.dst + unit_off(j), slot_uc(j), unit_len(j), tid);
+            }
+            if (k < K) {  // copy-in of unit k into the slot just emptied
+                copier_copy<T>(slot_uc(k), a.src + unit_off(k), unit_len(k), tid);
+                mbar_arrive(&full[k & 1]);
+            }
+        }
+        return;
+    }
+
+    // reducers (no early exit: every reducer reaches every named barrier)
+    const int rt = tid - kNvlsCopiers;
+    constexpr int U = 4;  // multimem units in flight per thread
     const size_t ctr_a = (size_t)b * kNvlsCtrStride;
     const size_t ctr_b = ((size_t)kMaxBlocks + b) * kNvlsCtrStride;
-    constexpr int U = 4;  // multimem units in flight per thread
     uint32_t k = 0;
-    for (;; ++k) {
-        const size_t off = ((size_t)k * G + b) * a.unit;
-        if (off >= a.bytes) break;  // the same on every rank
-        const size_t n = min(a.unit, a.bytes - off);
+    for (; k < K; ++k) {
         const uint32_t target = (base + k + 1) * (uint32_t)a.P;
-
-        // 1. copy-in, 2. meet on A
-        cta_copy<T>(slot_uc, a.src + off, n);
-        __syncthreads();
-        if (threadIdx.x == 0 && !nvls_meet(a, ctr_a, target, b, 0)) s_fail = 1;
-        __syncthreads();
-        if (s_fail) return;
+        if (!mbar_wait(&full[k & 1], (k >> 1) & 1, globaltimer() + 4 * a.timeout_ns, fail)) *fail = 1;
+        if (tid == kNvlsLeader && !*fail && !nvls_meet(a, ctr_a, target, b, 0)) *fail = 1;
+        asm volatile("bar.sync 1, %0;" ::"n"(kNvlsReducers) : "memory");
+        if (*fail) break;
         fence_proxy_alias();
-
-        // 3. this rank's share of the unit through the switch; the last
-        //    multimem unit may reach past n into the slot's padding, which is
-        //    never copied out
-        const size_t units = (n + M::bytes - 1) / M::bytes;
-        const size_t lo = units * a.rank / a.P, hi = units * (a.rank + 1) / a.P;
-        for (size_t u = lo + threadIdx.x; u < hi; u += U * blockDim.x) {
+        // this rank's share of the unit through the switch; the last multimem
+        // unit may reach past the data into the slot's padding, which is
+        // never copied out
+        const size_t n = unit_len(k);
+        const size_t mu = (n + M::bytes - 1) / M::bytes;
+        const size_t lo = mu * a.rank / a.P, hi = mu * (a.rank + 1) / a.P;
+        char *mc = slot_mc(k);
+        for (size_t u = lo + rt; u < hi; u += U * kNvlsReducers) {
             typename M::V v[U];
 #pragma unroll
             for (int q = 0; q < U; ++q)
-                if (u + q * blockDim.x < hi) v[q] = M::ld(slot_mc + (u + q * blockDim.x) * M::bytes);
+                if (u + q * kNvlsReducers < hi) v[q] = M::ld(mc + (u + q * kNvlsReducers) * M::bytes);
 #pragma unroll
             for (int q = 0; q < U; ++q)
-                if (u + q * blockDim.x < hi) M::st(slot_mc + (u + q * blockDim.x) * M::bytes, v[q]);
+                if (u + q * kNvlsReducers < hi) M::st(mc + (u + q * kNvlsReducers) * M::bytes, v[q]);
         }
-
-        // 4. meet on B, 5. copy-out
-        __syncthreads();
-        if (threadIdx.x == 0 && !nvls_meet(a, ctr_b, target, b, 1)) s_fail = 1;
-        __syncthreads();
-        if (s_fail) return;
-        fence_proxy_alias();
-        cta_copy<T>(a.dst + off, slot_uc, n);
+        asm volatile("bar.sync 2, %0;" ::"n"(kNvlsReducers) : "memory");
+        if (tid == kNvlsLeader) {
+            if (!nvls_meet(a, ctr_b, target, b, 1)) *fail = 1;
+            mbar_arrive(&done[k & 1]);  // also on failure: the copiers then see the flag
+        }
     }
-    if (threadIdx.x == 0) a.steps[b] = base + k;
+    if (tid == kNvlsLeader && !*fail) a.steps[b] = base + K;
 }
 
 // ---------------------------------------------------------------- fold

@@ -126,31 +126,31 @@ struct PushArgs {
 
 // NVLS allreduce through NVSwitch multicast, one independent pipeline per
 // CTA.  The message is cut into units of `unit` bytes; CTA b handles units
-// b, b + G, b + 2G, ... and owns one staging slot of `unit` bytes in the
-// multicast-bound region of every GPU.  For each of its units it
-//   1. copies the unit from the input into its slot (local HBM),
-//   2. meets CTA b of every other rank: fence, one multimem.red.release that
-//      adds 1 to its counter A[b] on every GPU, then waits until this GPU's
-//      copy of A[b] shows all P arrivals for this step,
-//   3. reduces this rank's 1/P of the unit with multimem.ld_reduce through
-//      the multicast view and broadcasts it with multimem.st,
-//   4. meets the others again on counter B[b] (every rank's share is now in
-//      every GPU's slot),
-//   5. copies the reduced unit from its slot into the output.
-// Different CTA indices never wait on one another, so the copies of some
-// CTAs overlap the multimem traffic of others without a grid-wide barrier.
-// One slot per CTA suffices: a rank refills its slot (step k + 1) only after
-// barrier B of step k, and the peers touch it again only after barrier A of
-// step k + 1, which needs that refill.  Counters only grow: steps[b] (this
-// GPU's unicast memory, the same on every GPU) holds the steps CTA b has
-// completed in earlier calls, so step k of this call is complete at
-// (steps[b] + k + 1) * P arrivals.  Counters are kNvlsCtrStride bytes apart.
+// b, b + G, b + 2G, ... through two staging slots of `unit` bytes in the
+// multicast-bound region of every GPU.  For each of its units k:
+//   1. copier warps copy the unit from the input into slot k % 2 (local HBM),
+//   2. the leader meets CTA b of every other rank: fence, one
+//      multimem.red.release that adds 1 to its counter A[b] on every GPU,
+//      then a wait until this GPU's copy of A[b] shows all P arrivals,
+//   3. reducer warps reduce this rank's 1/P of the unit with
+//      multimem.ld_reduce through the multicast view and broadcast it with
+//      multimem.st,
+//   4. the leader meets the others again on counter B[b] (every rank's share
+//      is now in every GPU's slot),
+//   5. copier warps copy the reduced unit from the slot into the output.
+// Copier warps run one unit ahead (copy-in of k + 1, copy-out of k - 1)
+// while the reducers work on unit k, and different CTA indices never wait on
+// one another, so local copies overlap the NVLink traffic without a
+// grid-wide barrier.  Counters only grow: steps[b] (this GPU's unicast
+// memory, the same on every GPU) holds the units CTA b completed in earlier
+// calls, so unit k of this call is complete at (steps[b] + k + 1) * P
+// arrivals.  Counters are kNvlsCtrStride bytes apart.
 constexpr int kNvlsCtrStride = 128;
 constexpr size_t kNvlsCtrBytes = 2 * (size_t)kMaxBlocks * kNvlsCtrStride;  // A and B counters
 struct NvlsArgs {
     const char *src;                 // this rank's input (user buffer)
     char *dst;                       // this rank's output (user buffer)
-    char *uc;                        // unicast view of slot 0 (slot b at uc + b * unit)
+    char *uc;                        // unicast view of slot 0 (CTA b's slots at uc + (2b + s) * unit)
     char *mc;                        // multicast view of slot 0
     char *mc_ctr;                    // multicast view of the counters (A[b], then B[b])
     const char *uc_ctr;              // this GPU's unicast view of the counters
