@@ -217,6 +217,7 @@ struct cail_dev_comm {
     MPI_Comm comm = MPI_COMM_NULL;
     bool ok = false;
     bool broken = false;
+    bool shared_gpu = false;  // test mode: ranks share a GPU (zero-copy two-shot only)
     int rank = 0, P = 1, dev = -1, sms = 148;
     cudaStream_t stream = nullptr;
     // workspace
@@ -700,6 +701,22 @@ size_t push_piece_min_env() {
     return v;
 }
 
+// CAIL_TEST_SHARED_GPU=1 (tests only): a communicator whose ranks share a
+// GPU still gets the NVLink runtime, so that a one-GPU test run exercises
+// the cross-process IPC, the registration cache and the P > 1 slicing of
+// the zero-copy two-shot.  Only that path (and the copy-engine two-shot)
+// then runs: its kernels never wait on another rank's kernel, the ranks
+// meet on the host.  The one-shot, push and NVLS kernels wait on their
+// peers' flags and must not run as separate processes on one GPU (nothing
+// makes such kernels run at the same time), so they are replaced by it.
+bool test_shared_gpu() {
+    static const bool v = [] {
+        const char *e = getenv("CAIL_TEST_SHARED_GPU");
+        return e && *e && *e != '0';
+    }();
+    return v;
+}
+
 cail_dev_comm *create_context(MPI_Comm comm) {
     auto *dc = new cail_dev_comm();
     dc->comm = comm;
@@ -731,16 +748,22 @@ cail_dev_comm *create_context(MPI_Comm comm) {
         ok = false;
     bool all_nvls = true;
     ok = ok && dc->P <= kMaxRanks;
+    const bool shared_ok = test_shared_gpu();
     for (int q = 0; ok && q < dc->P; ++q) {
         dc->peer_pid[q] = all[q].pid;
         if (all[q].host != me.host) ok = false;
         if (!all[q].nvls_capable) all_nvls = false;
         for (int r = 0; r < q; ++r)
-            if (memcmp(all[q].uuid, all[r].uuid, 16) == 0) ok = false;  // shared GPU
+            if (memcmp(all[q].uuid, all[r].uuid, 16) == 0) {  // shared GPU
+                if (shared_ok) dc->shared_gpu = true;
+                else ok = false;
+            }
         if (q == dc->rank) continue;
         int o = find_ordinal(all[q].uuid), can = 0;
+        if (o == dc->dev && shared_ok) continue;  // same device: reached through IPC without peer access
         if (o < 0 || cudaDeviceCanAccessPeer(&can, dc->dev, o) != cudaSuccess || !can) ok = false;
     }
+    if (dc->shared_gpu) all_nvls = false;
     dc->sms = me.sms > 0 ? me.sms : 148;
     if (!agree(comm, ok)) {
         CAIL_DBG("nvlink path unavailable on this communicator (probe)");
@@ -1124,6 +1147,13 @@ int ce_body(cail_dev_comm *dc, const char *const *srcs, char *const *dsts, size_
     return check_status(dc, "ce_two_shot");
 }
 
+// A datatype of storage class ec (the reduction depends only on the class).
+cail_datatype_t dtype_of_class(int ec) {
+    static const cail_datatype_t t[CAIL_EC_NUM] = {CAIL_CHAR, CAIL_UCHAR, CAIL_SHORT, CAIL_USHORT, CAIL_INT,
+                                                   CAIL_UINT, CAIL_LONG_LONG, CAIL_ULONGLONG, CAIL_FLOAT, CAIL_DOUBLE};
+    return ec >= 0 && ec < CAIL_EC_NUM ? t[ec] : CAIL_INVALID;
+}
+
 // 1 if a peer published kXErr in its arrive (depart) word for this call.
 bool peer_failed(const cail_dev_comm *dc, bool depart) {
     for (int q = 0; q < dc->P; ++q) {
@@ -1178,7 +1208,14 @@ int run_twoshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     if (!all_ok) {
         // some rank's buffer cannot be exported: every rank sees the same
         // descriptors and takes the copy-in path instead
-        rc = run_oneshot(dc, src, dst, count, esz, op, ec, false);
+        if (dc->shared_gpu) {
+            // (test mode, ranks on one GPU: no kernel that waits on peers)
+            rc = PMPI_Allreduce(src == dst ? MPI_IN_PLACE : src, dst, (int)count,
+                                cail_dtype_to_mpi_type(dtype_of_class(ec)),
+                                cail_optype_to_mpi_op((cail_op_t)op), dc->comm);
+        } else {
+            rc = run_oneshot(dc, src, dst, count, esz, op, ec, false);
+        }
     } else {
         cail::TwoShotArgs a;
         memset(&a, 0, sizeof(a));
@@ -1439,6 +1476,7 @@ int cail_dev_nvls_ok(cail_dev_comm *dc, cail_datatype_t dt, cail_op_t op) {
 
 int cail_dev_pick_algo(cail_dev_comm *dc, size_t bytes, int count, cail_datatype_t dt, cail_op_t op) {
     (void)count;
+    if (dc->shared_gpu) return CAIL_ALGO_TWO_SHOT;  // test mode: the only kernel that may share a GPU
     return pick_nvlink(dc->P, bytes, cail_dev_nvls_ok(dc, dt, op) != 0);
 }
 
@@ -1486,8 +1524,9 @@ int cail_dev_allreduce(cail_dev_comm *dc, int algo, const void *sendbuf, void *r
         cudaStreamWaitEvent(dc->stream, dc->legacy_ev, 0);
     }
     cail_prof_mark(CAIL_PH_SETUP, ts);
-    // A single rank runs the same kernels (they degenerate to a copy).
-    if (algo == CAIL_ALGO_ONE_SHOT) {
+    if (dc->shared_gpu && algo != CAIL_ALGO_CE_TWO_SHOT) {
+        rc = run_twoshot(dc, src, dst, (size_t)count, esz, (int)op, ec);  // ranks share a GPU (test mode)
+    } else if (algo == CAIL_ALGO_ONE_SHOT) {
         rc = run_oneshot(dc, src, dst, (size_t)count, esz, (int)op, ec, true);
     } else if (algo == CAIL_ALGO_NVLS && cail_dev_nvls_ok(dc, dt, op)) {
         rc = run_nvls(dc, src, dst, (size_t)count, esz, (int)op, ec, true);

@@ -121,6 +121,26 @@ def test_single_rank_copy_unaligned_views(copy_max):
     assert "views ok True copy" in r.stdout, r.stdout + r.stderr
 
 
+@pytest.mark.parametrize("np", [2, 3])
+def test_zero_copy_two_shot_with_ranks_sharing_one_gpu(np):
+    """CAIL_TEST_SHARED_GPU=1: 2 and 3 ranks on one GPU take the zero-copy
+    two-shot (the auto path above the one-shot crossover), whose kernels
+    never wait on one another: cross-process IPC of the user buffers, the
+    registration cache (64 rotating buffers, in place on every other call)
+    and the P > 1 slicing, bit for bit against PMPI."""
+    need_gpus(1)
+    env = {"CAIL_TEST_SHARED_GPU": "1", "CAIL_MIN_MSG_SIZE": "0", "CUDA_VISIBLE_DEVICES": "0", "CAIL_STATS": "1",
+           "CAIL_NVLS": "0"}
+    r = mpirun(np, ["cail_check", "-m", "matrix", "-c", "4099", "-d", "-p", "--bits"], preload="cuda", env=env,
+               timeout=900)
+    assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+    assert "two_shot=0 " not in r.stderr and "two_shot=" in r.stderr
+    r = mpirun(np, ["cail_check", "-m", "stress", "-c", "300000", "-r", "200", "-b", "64", "-d", "--bits"],
+               preload="cuda", env=env, timeout=900)
+    assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
+    assert "reg_hits=0 " not in r.stderr
+
+
 def test_device_wait_timeout_reports_status():
     """A one-shot kernel whose peer never arrives gives up after the limit
     and reports code 1; the context stays usable afterwards."""
