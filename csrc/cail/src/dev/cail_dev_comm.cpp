@@ -132,7 +132,7 @@ constexpr size_t kDefaultPieceMin = 4 << 10;             // push two-shot: small
 constexpr size_t kOsPieceMin = 8 << 10;                  // one-shot: smallest piece
 constexpr size_t kNvlsStepsOff = cail::kNvlsStepsBase * sizeof(uint32_t);
 constexpr size_t kNvlsCtrRegion = (cail::kNvlsCtrBytes + 65535) / 65536 * 65536;  // counters, then staging
-constexpr size_t kDefaultNvlsUnit = 256 << 10;          // NVLS: largest bytes per CTA and step
+constexpr size_t kDefaultNvlsUnit = 1 << 20;            // NVLS: largest bytes per CTA and step
 
 // ---------------------------------------------------------------- host exchange
 struct BufDesc {
@@ -523,16 +523,18 @@ bool nvls_step(cail_dev_comm *dc, bool ok, CUresult r, const char *what) {
 }
 
 int nvls_min_ranks();
+int nvls_min_ranks_env();
 
-// The multicast region (a 512 MiB granule per GPU) is created only where it
-// can be used: CAIL_ALGO=nvls, or auto mode with CAIL_NVLS_MIN_RANKS <= P or
-// a CAIL_TUNE_FILE line for P that gives nvls_min.
+// The multicast region (2 staging slots per CTA, ~592 MiB per GPU with 1 MiB
+// units) is created only where it can be used: CAIL_ALGO=nvls, or auto mode
+// from the built-in 8 ranks (or CAIL_NVLS_MIN_RANKS), or a CAIL_TUNE_FILE
+// line for P that gives nvls_min.
 bool nvls_wanted(int P) {
     if (!cail_global_state.nvls || P < 2) return false;
     if (cail_global_state.force_algo == CAIL_ALGO_NVLS) return true;
-    if (nvls_min_ranks() > 0) return P >= nvls_min_ranks();
     const cail_tune_t *t = cail_tune_for(P);
-    return t && t->nvls_min >= 0;
+    if (nvls_min_ranks_env() < 0 && t) return t->nvls_min >= 0;
+    return nvls_min_ranks() > 0 && P >= nvls_min_ranks();
 }
 
 void nvls_setup(cail_dev_comm *dc, bool all_capable) {
@@ -1320,7 +1322,10 @@ int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
     unit = unit <= (16 << 10) ? (16 << 10) : (unit + 65535) / 65536 * 65536;
     if (unit > dc->nvls_unit) unit = dc->nvls_unit;
     const size_t units = (bytes + unit - 1) / unit;
-    const int blocks = (int)(units < (size_t)G ? units : (size_t)G);
+    // as few CTAs as still give every CTA the same number of units (1 GiB of
+    // 1 MiB units: 256 CTAs of 4 units, not 296 CTAs of 3 or 4)
+    const size_t per = (units + G - 1) / G;
+    const int blocks = (int)((units + per - 1) / per);
     cail::NvlsArgs a;
     memset(&a, 0, sizeof(a));
     a.src = src;
@@ -1388,16 +1393,19 @@ size_t default_oneshot_max(int P) {
 
 // NVLS moves about N(1 + 1/P) bytes per GPU and direction plus a local
 // copy-in and copy-out, against 2N(P-1)/P for two-shot: it can only win at
-// large P.  Measured on B200 (1 GiB, float sum) it stays below two-shot at
-// every rank count: 311 vs 670 GB/s bus bandwidth at 2 ranks, 503 vs 670 at
-// 4, 594 vs 616-646 at 8.  multimem.ld_reduce + multimem.st alone move 544
-// GB/s per direction at 8 ranks, and the staging copies cost the rest.  So
-// auto mode uses NVLS only when CAIL_NVLS_MIN_RANKS (default 0: never) is
-// set and reached, from CAIL_NVLS_MIN bytes (default 16 MiB).
+// large P and large messages.  Measured on B200 (float sum, 1 MiB units):
+// 8 ranks, 713 GB/s bus bandwidth at 1 GiB against 650 for the zero-copy
+// two-shot, but 637 vs 656 at 512 MiB and 550 vs 641 at 256 MiB; 2 ranks,
+// 354 vs 659 at 1 GiB.  Built in: NVLS from 8 ranks and 1 GiB.
+// CAIL_NVLS_MIN_RANKS (0: never) and CAIL_NVLS_MIN (bytes) replace both
+// bounds; a CAIL_TUNE_FILE line for P replaces them for that rank count.
+constexpr int kNvlsDefaultMinRanks = 8;
+constexpr size_t kNvlsDefaultMinBytes = (size_t)1 << 30;
+
 size_t nvls_min_bytes() {
     static const size_t v = [] {
         const char *e = getenv("CAIL_NVLS_MIN");
-        return e ? (size_t)atoll(e) : (size_t)16 << 20;
+        return e && *e ? (size_t)atoll(e) : kNvlsDefaultMinBytes;
     }();
     return v;
 }
@@ -1412,12 +1420,20 @@ size_t ce_min_bytes() {
     return v;
 }
 
-int nvls_min_ranks() {
+// CAIL_NVLS_MIN_RANKS, or -1 when it is not set.
+int nvls_min_ranks_env() {
     static const int v = [] {
         const char *e = getenv("CAIL_NVLS_MIN_RANKS");
-        return e ? atoi(e) : 0;
+        return e && *e ? atoi(e) : -1;
     }();
     return v;
+}
+
+// Smallest rank count for which auto mode uses NVLS (0: never) on a
+// communicator of P ranks without a tune-file line.
+int nvls_min_ranks() {
+    const int e = nvls_min_ranks_env();
+    return e >= 0 ? e : kNvlsDefaultMinRanks;
 }
 
 // Auto mode on an NVLink communicator of P ranks; nvls_pair: NVLS is set up
@@ -1434,9 +1450,9 @@ int pick_nvlink(int P, size_t bytes, bool nvls_pair) {
                                                   : default_oneshot_max(P);
     if (bytes <= one_max) return CAIL_ALGO_ONE_SHOT;
     if (nvls_pair) {
-        if (nvls_min_ranks() > 0) {
-            if (P >= nvls_min_ranks() && bytes >= nvls_min_bytes()) return CAIL_ALGO_NVLS;
-        } else if (t && t->nvls_min >= 0 && bytes >= (size_t)t->nvls_min) {
+        if (nvls_min_ranks_env() < 0 && t) {
+            if (t->nvls_min >= 0 && bytes >= (size_t)t->nvls_min) return CAIL_ALGO_NVLS;
+        } else if (nvls_min_ranks() > 0 && P >= nvls_min_ranks() && bytes >= nvls_min_bytes()) {
             return CAIL_ALGO_NVLS;
         }
     }

@@ -46,7 +46,7 @@ def query(cases, env=None, stderr=None):
 def test_default_crossover_per_rank_count_and_two_shot_above():
     # measured: one_shot up to 64 KiB at 2 ranks, up to 256 KiB at 4 and 8
     cases = [(8, 32 * KIB, "MPI_FLOAT", "MPI_SUM"), (8, 256 * KIB, "MPI_FLOAT", "MPI_SUM"),
-             (8, 256 * KIB + 4, "MPI_FLOAT", "MPI_SUM"), (8, GIB, "MPI_FLOAT", "MPI_SUM"),
+             (8, 256 * KIB + 4, "MPI_FLOAT", "MPI_SUM"), (8, GIB - 4, "MPI_FLOAT", "MPI_SUM"),
              (2, 64 * KIB, "MPI_FLOAT", "MPI_SUM"), (2, 64 * KIB + 4, "MPI_FLOAT", "MPI_SUM"),
              (2, GIB, "MPI_DOUBLE", "MPI_MAX"), (4, 256 * KIB, "MPI_INT", "MPI_PROD"),
              (4, 16 * MIB, "MPI_INT", "MPI_PROD")]
@@ -66,16 +66,21 @@ def test_oneshot_max_and_small_threshold_move_the_crossover():
     assert query(cases, {"CAIL_MSG_SMALL_THRESHOLD": "262144"}) == ["one_shot", "two_shot"]
 
 
-def test_nvls_only_when_requested_and_for_multimem_pairs():
+def test_nvls_from_8_ranks_and_1_gib_and_only_for_multimem_pairs():
+    # built in (measured): NVLS from 8 ranks and 1 GiB, for the pairs multimem reduces
+    big = [(8, GIB, "MPI_FLOAT", "MPI_SUM"), (8, GIB - 4, "MPI_FLOAT", "MPI_SUM"),
+           (4, GIB, "MPI_FLOAT", "MPI_SUM"), (8, GIB, "MPI_FLOAT", "MPI_PROD"),
+           (8, GIB, "MPI_INT8_T", "MPI_SUM"), (8, GIB, "MPI_FLOAT", "MPI_MAX"),
+           (8, GIB, "MPI_INT", "MPI_MAX"), (8, GIB, "MPI_DOUBLE", "MPI_SUM")]
+    assert query(big) == ["nvls", "two_shot", "two_shot", "two_shot", "two_shot", "two_shot", "nvls", "nvls"]
+    assert query(big[:1], {"CAIL_NVLS": "0"}) == ["two_shot"]
+    assert query(big[:1], {"CAIL_NVLS_MIN_RANKS": "0"}) == ["two_shot"]
+    # the environment moves both bounds
     cases = [(8, 16 * MIB, "MPI_FLOAT", "MPI_SUM"), (8, 16 * MIB - 4, "MPI_FLOAT", "MPI_SUM"),
-             (4, 16 * MIB, "MPI_FLOAT", "MPI_SUM"), (8, 16 * MIB, "MPI_FLOAT", "MPI_PROD"),
-             (8, 16 * MIB, "MPI_INT8_T", "MPI_SUM"), (8, 16 * MIB, "MPI_FLOAT", "MPI_MAX"),
-             (8, 16 * MIB, "MPI_INT", "MPI_MAX"), (8, 16 * MIB, "MPI_DOUBLE", "MPI_SUM")]
-    assert query(cases) == ["two_shot"] * 8
-    assert query(cases, {"CAIL_NVLS_MIN_RANKS": "8"}) == [
-        "nvls", "two_shot", "two_shot", "two_shot", "two_shot", "two_shot", "nvls", "nvls"]
-    assert query(cases[:1], {"CAIL_NVLS_MIN_RANKS": "8", "CAIL_NVLS": "0"}) == ["two_shot"]
-    assert query(cases[:1], {"CAIL_NVLS_MIN_RANKS": "8", "CAIL_NVLS_MIN": str(64 * MIB)}) == ["two_shot"]
+             (4, 16 * MIB, "MPI_FLOAT", "MPI_SUM")]
+    assert query(cases) == ["two_shot"] * 3
+    assert query(cases, {"CAIL_NVLS_MIN": str(16 * MIB)}) == ["nvls", "two_shot", "two_shot"]
+    assert query(cases, {"CAIL_NVLS_MIN": str(16 * MIB), "CAIL_NVLS_MIN_RANKS": "4"}) == ["nvls", "two_shot", "nvls"]
 
 
 def test_copy_engine_two_shot_only_above_ce_min():
