@@ -809,24 +809,40 @@ __global__ void __launch_bounds__(512) fold_kernel(FoldArgs a) {
 }
 
 // ---------------------------------------------------------------- copy
-// One-rank allreduce: dst = src.  Loads bypass L1 (ld.global.nc, no L1
-// allocation) and stores are marked evict-first (st.global.cs): the data is
-// touched once.  Each thread keeps eight 16-byte loads in flight before it
-// stores them, which measured 0.0237 ms for 64 MiB on B200 against 0.0292 ms
-// for cudaMemcpyAsync and 0.0317 ms for one vector per iteration.
-__device__ __forceinline__ uint4 ld_v4_stream(const void *p) {
+// One-rank allreduce: dst = src.  Each thread keeps eight 16-byte loads in
+// flight before it stores them.  STREAM (messages whose source and
+// destination do not both fit in L2): loads bypass L1 (ld.global.nc, no L1
+// allocation) and stores are marked evict-first (st.global.cs), which
+// measured 0.0237 ms for 64 MiB on B200 against 0.0292 ms for
+// cudaMemcpyAsync.  Otherwise plain cached stores: with both buffers in the
+// 126 MB L2, evict-first stores only force write-backs that a cached copy
+// avoids (16 MiB, blocking call: 16.0 us with streaming hints against
+// 13.4-14.6 us for cudaMemcpy).
+template <bool STREAM>
+__device__ __forceinline__ uint4 ld_v4_copy(const void *p) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
+    if constexpr (STREAM)
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(p));
+    else
+        asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(p));
     return v;
 }
 
-__device__ __forceinline__ void st_v4_stream(void *p, uint4 v) {
-    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                 : "memory");
+template <bool STREAM>
+__device__ __forceinline__ void st_v4_copy(void *p, uint4 v) {
+    if constexpr (STREAM)
+        asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
+    else
+        asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
 }
 
+template <bool STREAM>
 __global__ void __launch_bounds__(512) copy_kernel(char *dst, const char *src, size_t head, size_t nvec,
                                                    size_t bytes) {
     constexpr int U = 8;
@@ -838,11 +854,11 @@ __global__ void __launch_bounds__(512) copy_kernel(char *dst, const char *src, s
     for (; i + (U - 1) * stride < nvec; i += U * stride) {
         uint4 v[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) v[u] = ld_v4_stream(s + i + u * stride);
+        for (int u = 0; u < U; ++u) v[u] = ld_v4_copy<STREAM>(s + i + u * stride);
 #pragma unroll
-        for (int u = 0; u < U; ++u) st_v4_stream(d + i + u * stride, v[u]);
+        for (int u = 0; u < U; ++u) st_v4_copy<STREAM>(d + i + u * stride, v[u]);
     }
-    for (; i < nvec; i += stride) st_v4_stream(d + i, ld_v4_stream(s + i));
+    for (; i < nvec; i += stride) st_v4_copy<STREAM>(d + i, ld_v4_copy<STREAM>(s + i));
     // ragged head and tail (< 16 bytes each)
     if (tid < head) dst[tid] = src[tid];
     const size_t t0 = head + nvec * 16;
@@ -1044,7 +1060,11 @@ cudaError_t launch_copy(char *dst, const char *src, size_t bytes, int sm_count, 
     const size_t want = (nvec + 4 * threads - 1) / (4 * threads);
     const size_t cap = (size_t)(sm_count > 0 ? sm_count : 148) * 2;
     const int blocks = (int)(want < 1 ? 1 : (want > cap ? cap : want));
-    copy_kernel<<<blocks, threads, 0, s>>>(dst, src, head, nvec, bytes);
+    // streaming hints only when source and destination overflow the L2
+    if (bytes > ((size_t)48 << 20))
+        copy_kernel<true><<<blocks, threads, 0, s>>>(dst, src, head, nvec, bytes);
+    else
+        copy_kernel<false><<<blocks, threads, 0, s>>>(dst, src, head, nvec, bytes);
     return cudaGetLastError();
 }
 

@@ -8,6 +8,7 @@ order and is checked with a reassociation tolerance.
 """
 import ctypes
 import os
+import re
 import subprocess
 import sys
 
@@ -134,11 +135,13 @@ def test_zero_copy_two_shot_with_ranks_sharing_one_gpu(np):
     r = mpirun(np, ["cail_check", "-m", "matrix", "-c", "4099", "-d", "-p", "--bits"], preload="cuda", env=env,
                timeout=900)
     assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
-    assert "two_shot=0 " not in r.stderr and "two_shot=" in r.stderr
+    calls = [int(n) for n in re.findall(r"(?<![a-z_])two_shot=(\d+)", r.stderr)]
+    assert len(calls) == np and all(n > 0 for n in calls), r.stderr[-2000:]
     r = mpirun(np, ["cail_check", "-m", "stress", "-c", "300000", "-r", "200", "-b", "64", "-d", "--bits"],
                preload="cuda", env=env, timeout=900)
     assert ok(r), r.stdout[-3000:] + r.stderr[-3000:]
-    assert "reg_hits=0 " not in r.stderr
+    hits = [int(n) for n in re.findall(r"reg_hits=(\d+)", r.stderr)]
+    assert len(hits) == np and all(n > 0 for n in hits), r.stderr[-2000:]
 
 
 def test_device_wait_timeout_reports_status():
