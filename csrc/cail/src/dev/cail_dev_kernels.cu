@@ -1048,7 +1048,7 @@ int nvls_max_ctas(int sm_count) {
     return g > kMaxBlocks ? kMaxBlocks : g;
 }
 
-cudaError_t launch_copy(char *dst, const char *src, size_t bytes, int sm_count, cudaStream_t s) {
+cudaError_t launch_copy(char *dst, const char *src, size_t bytes, int sm_count, cudaStream_t s, bool stream) {
     if (bytes == 0) return cudaSuccess;
     if ((((uintptr_t)src ^ (uintptr_t)dst) & 15) != 0) return cudaErrorInvalidValue;
     size_t head = (16 - ((uintptr_t)src & 15)) & 15;
@@ -1060,8 +1060,7 @@ cudaError_t launch_copy(char *dst, const char *src, size_t bytes, int sm_count, 
     const size_t want = (nvec + 4 * threads - 1) / (4 * threads);
     const size_t cap = (size_t)(sm_count > 0 ? sm_count : 148) * 2;
     const int blocks = (int)(want < 1 ? 1 : (want > cap ? cap : want));
-    // streaming hints only when source and destination overflow the L2
-    if (bytes > ((size_t)48 << 20))
+    if (stream)
         copy_kernel<true><<<blocks, threads, 0, s>>>(dst, src, head, nvec, bytes);
     else
         copy_kernel<false><<<blocks, threads, 0, s>>>(dst, src, head, nvec, bytes);

@@ -201,7 +201,8 @@ int nvls_supported(int op, int ec);
 // Device-to-device copy of `bytes` bytes (the one-rank allreduce); src and dst
 // must share their alignment modulo 16.  16-byte vectors, eight loads in
 // flight per thread, at most two 512-thread CTAs per SM.
-cudaError_t launch_copy(char *dst, const char *src, size_t bytes, int sm_count, cudaStream_t s);
+// stream: streaming cache hints (messages whose buffers overflow L2).
+cudaError_t launch_copy(char *dst, const char *src, size_t bytes, int sm_count, cudaStream_t s, bool stream);
 // Element-wise local reduction io = op(io, in) (PMPI algorithm path).
 cudaError_t launch_reduce_local(int op, int ec, const void *in, void *io, size_t n, int sm_count,
                                 cudaStream_t s);

@@ -171,7 +171,13 @@ int cail_gpu_single_rank(const void *src, void *dst, size_t bytes) {
         e = cail::launch_bulk_copy((char *)dst, (const char *)src, bytes, g_sms[d], timeout_ns, g_copy_status_d[d], s);
         cail_counters.launches++;
     } else if (vec) {
-        e = cail::launch_copy((char *)dst, (const char *)src, bytes, g_sms[d], s);
+        // streaming hints only when source and destination overflow the L2
+        // (CAIL_COPY_STREAM_MIN bytes, default 48 MiB)
+        static const size_t stream_min = [] {
+            const char *v = getenv("CAIL_COPY_STREAM_MIN");
+            return v && *v ? (size_t)strtoull(v, nullptr, 10) : ((size_t)48 << 20);
+        }();
+        e = cail::launch_copy((char *)dst, (const char *)src, bytes, g_sms[d], s, bytes > stream_min);
         cail_counters.launches++;
     } else {
         e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s);

@@ -291,7 +291,7 @@ extern "C" int cail_bench_kernel_local(int kernel, int P, size_t bytes, int iter
         fill_pattern<<<1024, 256, 0, s>>>((uint32_t *)src, bytes / 4);
         auto launch = [&]() {
             return kernel == 3 ? cail::launch_bulk_copy(dst, src, bytes, sms, 2000000000ull, bst, s)
-                               : cail::launch_copy(dst, src, bytes, sms, s);
+                               : cail::launch_copy(dst, src, bytes, sms, s, bytes > ((size_t)48 << 20));
         };
         if (launch() != cudaSuccess) { rc = -1; goto out; }
         cudaEventRecord(e0, s);
