@@ -1383,11 +1383,13 @@ bool twoshot_zero_copy(const cail_dev_comm *dc) {
 
 // Built-in one_shot / two_shot crossover per rank count, measured on B200
 // (blocking calls, float sum): 2 ranks, one-shot and zero-copy two-shot
-// equal up to 64 KiB (20.2 us), two-shot ahead from 128 KiB; 8 ranks,
-// one-shot ahead up to 256 KiB (28.2 vs 29.0 us), two-shot from 512 KiB
-// (27.8 vs 31.8 us).  CAIL_TUNE_FILE lines replace it per rank count.
+// equal up to 64 KiB (20.2 us), two-shot ahead from 128 KiB; 4 ranks, equal
+// at 64 KiB (23.6 vs 23.9 us), two-shot ahead from 128 KiB (24.4 vs 26.1 us
+// at 256 KiB); 8 ranks, one-shot ahead up to 256 KiB (28.2 vs 29.0 us),
+// two-shot from 512 KiB (27.8 vs 31.8 us).  CAIL_TUNE_FILE lines replace it
+// per rank count.
 size_t default_oneshot_max(int P) {
-    if (P <= 2) return 64 << 10;
+    if (P <= 4) return 64 << 10;
     return 256 << 10;
 }
 

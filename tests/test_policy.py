@@ -44,12 +44,12 @@ def query(cases, env=None, stderr=None):
 
 
 def test_default_crossover_per_rank_count_and_two_shot_above():
-    # measured: one_shot up to 64 KiB at 2 ranks, up to 256 KiB at 4 and 8
+    # measured: one_shot up to 64 KiB at 2 and 4 ranks, up to 256 KiB at 8
     cases = [(8, 32 * KIB, "MPI_FLOAT", "MPI_SUM"), (8, 256 * KIB, "MPI_FLOAT", "MPI_SUM"),
              (8, 256 * KIB + 4, "MPI_FLOAT", "MPI_SUM"), (8, GIB - 4, "MPI_FLOAT", "MPI_SUM"),
              (2, 64 * KIB, "MPI_FLOAT", "MPI_SUM"), (2, 64 * KIB + 4, "MPI_FLOAT", "MPI_SUM"),
-             (2, GIB, "MPI_DOUBLE", "MPI_MAX"), (4, 256 * KIB, "MPI_INT", "MPI_PROD"),
-             (4, 16 * MIB, "MPI_INT", "MPI_PROD")]
+             (2, GIB, "MPI_DOUBLE", "MPI_MAX"), (4, 64 * KIB, "MPI_INT", "MPI_PROD"),
+             (4, 256 * KIB, "MPI_INT", "MPI_PROD")]
     assert query(cases) == ["one_shot", "one_shot", "two_shot", "two_shot", "one_shot", "two_shot", "two_shot",
                             "one_shot", "two_shot"]
 
