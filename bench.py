@@ -67,6 +67,8 @@ class Comm:
 
     def barrier(self):
         if self.impl == "nccl":
+            if self.size == 1:  # one rank: no process group is created
+                return
             import torch.distributed as dist
             dist.barrier()
         else:
@@ -75,6 +77,8 @@ class Comm:
 
     def max(self, v: float) -> float:
         if self.impl == "nccl":
+            if self.size == 1:
+                return v
             import torch
             import torch.distributed as dist
             t = torch.tensor([v], dtype=torch.float64, device="cuda")
