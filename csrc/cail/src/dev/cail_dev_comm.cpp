@@ -719,6 +719,54 @@ bool test_shared_gpu() {
     return v;
 }
 
+// Workspace sizing, the same on every rank.  Push two-shot: the largest
+// piece keeps its two areas (2 parities x G CTAs x P sources x piece each)
+// near 296 MiB (128 KiB at 2 ranks, 64 KiB at 4, 32 KiB at 8; larger pieces
+// amortise the flag round trips of each round) unless
+// CAIL_TWOSHOT_PIECE_MAX sets it.  One-shot: 3 slots x G x P x piece, about
+// 112 MiB (64 KiB pieces at 2 ranks, 16 KiB at 8).
+size_t push_piece_max_for(int P, int gmax) {
+    if (push_piece_max_env()) return push_piece_max_env();
+    size_t pm = ((size_t)296 << 20) / ((size_t)4 * gmax * P);
+    pm = pm / (16 << 10) * (16 << 10);
+    return std::min(std::max(pm, (size_t)16 << 10), (size_t)256 << 10);
+}
+size_t push_area_for(int P, int gmax, size_t piece_max) {
+    return ((size_t)2 * gmax * P * piece_max + 255) / 256 * 256;
+}
+size_t os_piece_max_for(int P, int gmax) {
+    size_t pm = ((size_t)112 << 20) / ((size_t)cail::kOsSlots * gmax * P);
+    pm = pm / (8 << 10) * (8 << 10);
+    return std::min(std::max(pm, kOsPieceMin), (size_t)256 << 10);
+}
+size_t os_area_for(int P, int gmax, size_t piece_max) {
+    return ((size_t)cail::kOsSlots * gmax * P * piece_max + 255) / 256 * 256;
+}
+
+// One-shot launch shape: pieces of at least 8 KiB so that small messages use
+// few CTAs (one vector per thread), at most the area's piece.
+void oneshot_shape(size_t bytes, int gmax, size_t piece_max, size_t *piece, int *G) {
+    size_t p = (bytes + gmax - 1) / gmax;
+    p = (p + 15) / 16 * 16;
+    p = std::min(std::max(p, kOsPieceMin), piece_max);
+    *piece = p;
+    *G = (int)std::max<size_t>(1, std::min<size_t>((bytes + p - 1) / p, (size_t)gmax));
+}
+
+// NVLS launch shape: units of at most unit_max bytes (16 KiB to 64 KiB
+// steps for small messages, so that every CTA has work), and as few CTAs as
+// still give every CTA the same number of units (1 GiB of 1 MiB units: 256
+// CTAs of 4 units, not 296 CTAs of 3 or 4).
+void nvls_shape(size_t bytes, int gmax, size_t unit_max, size_t *unit, int *blocks) {
+    size_t u = (bytes + gmax - 1) / gmax;
+    u = u <= (16 << 10) ? (16 << 10) : (u + 65535) / 65536 * 65536;
+    if (u > unit_max) u = unit_max;
+    const size_t units = (bytes + u - 1) / u;
+    const size_t per = (units + gmax - 1) / gmax;
+    *unit = u;
+    *blocks = (int)((units + per - 1) / per);
+}
+
 cail_dev_comm *create_context(MPI_Comm comm) {
     auto *dc = new cail_dev_comm();
     dc->comm = comm;
@@ -781,21 +829,10 @@ cail_dev_comm *create_context(MPI_Comm comm) {
     // ranks, 64 KiB at 4, 32 KiB at 8): larger pieces amortise the flag
     // round trips of each round
     dc->push_gmax = cail::push_max_ctas(1, dc->sms);
-    dc->push_piece_max = push_piece_max_env();
-    if (dc->push_piece_max == 0) {
-        size_t pm = ((size_t)296 << 20) / ((size_t)4 * dc->push_gmax * dc->P);
-        pm = pm / (16 << 10) * (16 << 10);
-        dc->push_piece_max = std::min(std::max(pm, (size_t)16 << 10), (size_t)256 << 10);
-    }
-    dc->push_area = ((size_t)2 * dc->push_gmax * dc->P * dc->push_piece_max + 255) / 256 * 256;
-    // one-shot area: 3 slots x G CTAs x P sources x the largest piece, about
-    // 112 MiB (64 KiB pieces at 2 ranks, 16 KiB at 8)
-    {
-        size_t pm = ((size_t)112 << 20) / ((size_t)cail::kOsSlots * dc->push_gmax * dc->P);
-        pm = pm / (8 << 10) * (8 << 10);
-        dc->os_piece_max = std::min(std::max(pm, kOsPieceMin), (size_t)256 << 10);
-        dc->os_area = ((size_t)cail::kOsSlots * dc->push_gmax * dc->P * dc->os_piece_max + 255) / 256 * 256;
-    }
+    dc->push_piece_max = push_piece_max_for(dc->P, dc->push_gmax);
+    dc->push_area = push_area_for(dc->P, dc->push_gmax, dc->push_piece_max);
+    dc->os_piece_max = os_piece_max_for(dc->P, dc->push_gmax);
+    dc->os_area = os_area_for(dc->P, dc->push_gmax, dc->os_piece_max);
     ok = ok && cudaMalloc(&dc->ws, kOsOff + dc->os_area + 2 * dc->push_area) == cudaSuccess;
     ok = ok && cudaMemset(dc->ws, 0, kFlagBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
     ok = ok && cudaHostAlloc((void **)&dc->status_h, sizeof(DevStatus), cudaHostAllocMapped) == cudaSuccess;
@@ -928,11 +965,8 @@ int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     const size_t bytes = count * esz;
     cail::OneShotArgs a;
     memset(&a, 0, sizeof(a));
-    const int gmax = dc->push_gmax;
-    size_t piece = (bytes + gmax - 1) / gmax;
-    piece = (piece + 15) / 16 * 16;
-    piece = std::min(std::max(piece, kOsPieceMin), dc->os_piece_max);
-    a.G = (int)std::max<size_t>(1, std::min<size_t>((bytes + piece - 1) / piece, (size_t)gmax));
+    size_t piece = 0;
+    oneshot_shape(bytes, dc->push_gmax, dc->os_piece_max, &piece, &a.G);
     a.piece = piece;
     a.bytes = bytes;
     a.area = dc->os_area;
@@ -1317,15 +1351,9 @@ depart:
 int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec,
              bool allow_ordered) {
     const size_t bytes = count * esz;
-    const int G = dc->nvls_blocks;
-    size_t unit = (bytes + G - 1) / G;
-    unit = unit <= (16 << 10) ? (16 << 10) : (unit + 65535) / 65536 * 65536;
-    if (unit > dc->nvls_unit) unit = dc->nvls_unit;
-    const size_t units = (bytes + unit - 1) / unit;
-    // as few CTAs as still give every CTA the same number of units (1 GiB of
-    // 1 MiB units: 256 CTAs of 4 units, not 296 CTAs of 3 or 4)
-    const size_t per = (units + G - 1) / G;
-    const int blocks = (int)((units + per - 1) / per);
+    size_t unit = 0;
+    int blocks = 0;
+    nvls_shape(bytes, dc->nvls_blocks, dc->nvls_unit, &unit, &blocks);
     cail::NvlsArgs a;
     memset(&a, 0, sizeof(a));
     a.src = src;
@@ -1568,6 +1596,52 @@ void cail_dev_finalize_all(void) {
     }
     g_contexts.clear();
     if (g_keyval != MPI_KEYVAL_INVALID) PMPI_Comm_free_keyval(&g_keyval);
+}
+
+// Test hook: the launch shape an NVLink path computes for a call, without a
+// GPU (the tests check its invariants over many sizes).  kind 0: one-shot,
+// out = {G, piece, area}; kind 1: push two-shot, out = {G, piece, rounds,
+// max_slice, area, slice_off[0..P]}; kind 2: NVLS, out = {blocks, unit,
+// staging bytes}.  gmax: CTAs per rank (two per SM on B200: 296); vec: the
+// buffers are 16-byte aligned.  Returns the number of values written, or -1.
+int cail_dev_plan(int kind, int P, size_t count, size_t esz, int vec, int gmax, unsigned long long *out, int nout) {
+    if (P < 2 || P > kMaxRanks || gmax < 1 || gmax > cail::kMaxBlocks || !out) return -1;
+    const size_t bytes = count * esz;
+    if (kind == 0) {
+        if (nout < 3) return -1;
+        size_t piece = 0;
+        int G = 0;
+        oneshot_shape(bytes, gmax, os_piece_max_for(P, gmax), &piece, &G);
+        out[0] = (unsigned long long)G;
+        out[1] = piece;
+        out[2] = os_area_for(P, gmax, os_piece_max_for(P, gmax));
+        return 3;
+    }
+    if (kind == 1) {
+        if (nout < 5 + P + 1) return -1;
+        cail::PushArgs a;
+        memset(&a, 0, sizeof(a));
+        const size_t pm = push_piece_max_for(P, gmax);
+        push_shape(a, P, count, esz, vec != 0, gmax, pm, push_piece_min_env());
+        out[0] = (unsigned long long)a.G;
+        out[1] = a.piece;
+        out[2] = (unsigned long long)a.rounds;
+        out[3] = a.max_slice;
+        out[4] = push_area_for(P, gmax, pm);
+        for (int q = 0; q <= P; ++q) out[5 + q] = a.slice_off[q];
+        return 5 + P + 1;
+    }
+    if (kind == 2) {
+        if (nout < 3) return -1;
+        size_t unit = 0;
+        int blocks = 0;
+        nvls_shape(bytes, gmax, kDefaultNvlsUnit, &unit, &blocks);
+        out[0] = (unsigned long long)blocks;
+        out[1] = unit;
+        out[2] = (unsigned long long)gmax * 2 * kDefaultNvlsUnit;
+        return 3;
+    }
+    return -1;
 }
 
 // Self-test of the bounded device wait, on one GPU: a one-shot kernel for
