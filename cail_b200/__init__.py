@@ -73,9 +73,10 @@ def last_algorithm() -> Optional[str]:
 
 
 def set_stream_ordered(on: bool) -> Optional[bool]:
-    """Stream-ordered completion of small (one-shot) allreduces: the call
-    returns once the kernel is queued and the legacy default stream waits for
-    it, as with NCCL; the default (False) is MPI's host-synchronous return.
+    """Stream-ordered completion of NVLink allreduces (one_shot, two_shot
+    through the push kernel, nvls): the call returns once the kernel is queued
+    and the legacy default stream waits for it, as with NCCL; the default
+    (False) is MPI's host-synchronous return.
     Returns the previous mode (None when the loaded interposer is not ours)."""
     libs = _lib.loaded()
     if libs is None or libs.impl != "ours":

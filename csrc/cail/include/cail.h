@@ -64,16 +64,18 @@ int cail_comm_uses_nvls(MPI_Comm comm);
  * kernels overlap later work on other streams.  Returns the previous mode. */
 int cail_set_stream_sync(int mode);
 
-/* Completion of small messages (the one-shot path on NVLink communicators).
+/* Completion of device calls on NVLink communicators.
  * 0 (default, env CAIL_STREAM_ORDERED): MPI_Allreduce returns when the result
- * is in the receive buffer, as MPI specifies.  1: it returns once the kernel
- * is queued and the legacy default stream has been made to wait for it, the
- * completion semantics of NCCL: work queued later on the legacy stream (and
- * cudaMemcpy, cudaDeviceSynchronize) sees the result, host reads of the
- * buffer without such a synchronisation do not.  Needs stream sync mode 1;
- * larger messages stay host-synchronous (their algorithms exchange buffers
- * on the host).  A device-side timeout of a stream-ordered call is reported
- * by the next call or at MPI_Finalize.  Returns the previous mode. */
+ * is in the receive buffer, as MPI specifies.  1: one_shot, two_shot and nvls
+ * calls return once their kernel is queued and the legacy default stream has
+ * been made to wait for it, the completion semantics of NCCL: work queued
+ * later on the legacy stream (and cudaMemcpy, cudaDeviceSynchronize) sees the
+ * result, host reads of the buffer without such a synchronisation do not.
+ * Two-shot calls then run the push kernel, which needs no host barrier (the
+ * zero-copy kernel, used otherwise, synchronises the host).  Needs stream sync
+ * mode 1; ce_two_shot stays host-synchronous.  A device-side timeout of a
+ * stream-ordered call is reported by the next call or at MPI_Finalize.
+ * Returns the previous mode. */
 int cail_set_stream_ordered(int mode);
 
 /* The algorithm auto mode picks for an intercepted device-buffer call of
