@@ -242,18 +242,23 @@ def test_nan_and_inf_max_min_bit_identical_to_pmpi():
 
 
 @pytest.mark.multigpu
-def test_stream_ordered_small_messages_bit_exact():
-    """CAIL_STREAM_ORDERED=1: one-shot calls return once queued and the legacy
-    stream waits for them; results read back through the legacy stream must
-    be the rank-order oracle's, also over 64 rotating buffers with in-place
-    calls interleaved."""
+@pytest.mark.parametrize("algo", ["one_shot", "two_shot", "nvls"])
+def test_stream_ordered_calls(algo):
+    """CAIL_STREAM_ORDERED=1: one_shot, two_shot (the push kernel, which needs
+    no host barrier) and nvls calls return once queued and the legacy stream
+    waits for them; results read back through the legacy stream must be the
+    rank-order oracle's (NVLS: within tolerance, the switch reassociates),
+    also over 64 rotating buffers with in-place calls interleaved, so that
+    successive calls reuse the workspace slots while earlier kernels may
+    still run."""
     need_gpus(2)
-    env = {"CAIL_ALGO": "one_shot", "CAIL_MIN_MSG_SIZE": "0", "CAIL_STREAM_ORDERED": "1"}
+    env = {"CAIL_ALGO": algo, "CAIL_MIN_MSG_SIZE": "0", "CAIL_STREAM_ORDERED": "1", "CAIL_STATS": "1"}
+    exact = ["--bits"] if algo != "nvls" else ["--tol", "1e-4"]
     for np in nranks():
-        r = mpirun(np, ["cail_check", "-m", "matrix", "-c", "4099", "-d", "-p", "--bits"], preload="cuda",
+        r = mpirun(np, ["cail_check", "-m", "matrix", "-c", "4099", "-d", "-p"] + exact, preload="cuda",
                    env=env, timeout=900)
         assert ok(r), f"np={np}\n" + r.stdout[-3000:] + r.stderr[-3000:]
-        r = mpirun(np, ["cail_check", "-m", "stress", "-c", "32768", "-r", "300", "-b", "64", "-d", "--bits"],
+        r = mpirun(np, ["cail_check", "-m", "stress", "-c", "300000", "-r", "300", "-b", "64", "-d"] + exact,
                    preload="cuda", env=env, timeout=900)
         assert ok(r), f"np={np}\n" + r.stdout[-3000:] + r.stderr[-3000:]
 
