@@ -10,7 +10,7 @@
 // nothing and each SM alternates long read and write bursts.  Measured on
 // B200 for 1 GiB: 0.326 ms, against 0.333 ms for cudaMemcpyAsync and 0.336 ms
 // for the best plain-load kernel (16 vectors in flight per thread); the
-// plain-load copy kernel stays faster below ~128 MiB.  No multicast is used:
+// plain-load copy kernel leads up to 64 MiB.  No multicast is used:
 // source and destination are this GPU's own memory.
 //
 // The unaligned head and the tail (< 16 bytes each) are copied with plain
