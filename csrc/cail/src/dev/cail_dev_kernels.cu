@@ -642,14 +642,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
     }
 }
 
-// n bytes with the copier threads (tid in [0, kNvlsCopiers)); 16-byte vectors
-// (four in flight per thread) when both ends are aligned.
+// n bytes with the copier threads (tid in [0, kNvlsCopiers)).  Thread tid
+// moves the 16-byte chunks tid, tid + kNvlsCopiers, ... of the unit, the
+// partial last chunk included, whatever the alignment of either end and the
+// unit's length.  The copy-out of a slot and the copy-in that refills it
+// therefore touch every slot byte from the same thread, in program order,
+// and need no barrier between them (a thread that wrote a chunk another
+// thread had not yet copied out would corrupt that unit's result).  Both
+// ends 16-byte aligned: whole chunks as vectors, four in flight per thread;
+// otherwise element by element inside the chunk (an element never straddles
+// two chunks: the slot and the unit's offset are 16-byte multiples).
 template <typename T>
 __device__ __forceinline__ void copier_copy(char *dst, const char *src, size_t n, int tid) {
-    size_t done = 0;
+    const size_t nv = n / 16;
     if ((((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
         constexpr int U = 4;
-        const size_t nv = n / 16;
         size_t i = tid;
         for (; i + (U - 1) * kNvlsCopiers < nv; i += U * kNvlsCopiers) {
             uint4 v[U];
@@ -659,10 +666,19 @@ __device__ __forceinline__ void copier_copy(char *dst, const char *src, size_t n
             for (int u = 0; u < U; ++u) st_v4(dst + (i + u * kNvlsCopiers) * 16, v[u]);
         }
         for (; i < nv; i += kNvlsCopiers) st_v4(dst + i * 16, ld_v4(src + i * 16));
-        done = nv * 16;
+    } else {
+        constexpr int E = 16 / (int)sizeof(T);
+        for (size_t i = tid; i < nv; i += kNvlsCopiers) {
+            T v[E];
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = reinterpret_cast<const T *>(src + i * 16)[e];
+#pragma unroll
+            for (int e = 0; e < E; ++e) reinterpret_cast<T *>(dst + i * 16)[e] = v[e];
+        }
     }
-    for (size_t e = done / sizeof(T) + tid; e < n / sizeof(T); e += kNvlsCopiers)
-        reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
+    if (nv % kNvlsCopiers == (size_t)tid)  // the partial last chunk (none when n is a multiple of 16)
+        for (size_t off = nv * 16; off < n; off += sizeof(T))
+            *reinterpret_cast<T *>(dst + off) = *reinterpret_cast<const T *>(src + off);
 }
 
 // One CTA per staging pair: copier warps move unit k + 1 in and unit k - 1
