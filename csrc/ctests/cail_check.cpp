@@ -7,7 +7,8 @@
 // compared with PMPI_Allreduce of the same inputs (integers bit-exact,
 // floats bit-exact or within a reassociation tolerance, see --tol).
 //
-//   cail_check -m basic|matrix|edge|config1|config3|stress|leave|canary_selftest|expect_error|stall|memkinds|nan
+//   cail_check -m basic|matrix|edge|slots|config1|config3|stress|leave|canary_selftest|expect_error|stall|
+//                 memkinds|nan
 //              [-c count] [-d] [-a algo]
 //              [-p] [-r reps] [--bits]
 //     -d      device buffers (cudaMalloc) instead of malloc
@@ -487,6 +488,25 @@ void mode_edge() {
 // seeded seed+rank and INT MAX 65536 uniform [-1000,1000], each algorithm x
 // {separate, in place}, compared with PMPI_Allreduce; min-msg-size fallback
 // at count 1024.
+// Large messages with a ragged end (a length that is not a multiple of 16
+// bytes) and with buffers one or three elements off a 16-byte boundary,
+// separate and in place.  Run with CAIL_ALGO=nvls and a small CAIL_NVLS_UNIT
+// they give each CTA several units, so its two staging slots are refilled
+// while earlier units are copied out.  count (default 10,485,763 floats,
+// 40 MiB + 12 bytes) sets the float and int cases; the 8-byte cases take
+// half of it, rounded to an odd count.
+void mode_slots(int count, double tol) {
+    const TypeCase &tf = kTypes[5], &td = kTypes[6], &ti = kTypes[2], &tu = kTypes[11];
+    const size_t n = count > 0 ? (size_t)count : 10485763;
+    const size_t h = (n / 2) | 1;
+    report(check_one(tf, kOps[0], n, false, 31, tol), "ragged float SUM count=" + std::to_string(n));
+    report(check_one(tf, kOps[0], n, false, 32, tol, 1), "unaligned float SUM count=" + std::to_string(n));
+    report(check_one(tf, kOps[0], n, true, 33, tol, 3), "unaligned float SUM in place count=" + std::to_string(n));
+    report(check_one(td, kOps[0], h, true, 34, tol, 1), "unaligned double SUM in place count=" + std::to_string(h));
+    report(check_one(ti, kOps[2], n, false, 35, 0, 1), "unaligned int MAX count=" + std::to_string(n));
+    report(check_one(tu, kOps[0], h, false, 36, 0), "ragged unsigned long long SUM count=" + std::to_string(h));
+}
+
 void mode_config1(double tol) {
     const char *algo = getenv("CAIL_ALGO");
     std::string a = algo ? algo : "auto";
@@ -627,6 +647,7 @@ int main(int argc, char **argv) {
     if (mode == "basic") mode_basic(count);
     else if (mode == "matrix") mode_matrix(count ? count : 1000, tol);
     else if (mode == "edge") mode_edge();
+    else if (mode == "slots") mode_slots(count, tol);
     else if (mode == "config3") mode_config3(tol);
     else if (mode == "config1") mode_config1(tol);
     else if (mode == "stress") mode_stress(count ? count : 4096, reps, nbuf, tol);

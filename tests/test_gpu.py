@@ -221,6 +221,23 @@ def test_nvlink_edge_and_config1():
 
 
 @pytest.mark.multigpu
+@pytest.mark.parametrize("algo", ["nvls", "two_shot", "two_shot_zerocopy", "one_shot"])
+def test_large_ragged_and_unaligned_messages(algo):
+    """Messages of 40 MiB plus a few bytes (not a multiple of 16 bytes), on
+    buffers one or three elements off a 16-byte boundary, separate and in
+    place.  With 64 KiB NVLS units every CTA refills its two staging slots
+    while earlier units are still being copied out; the P2P kernels run many
+    rounds.  Integers bit-exact, floats bit-exact on the P2P kernels and
+    within reassociation tolerance on NVLS."""
+    need_gpus(2)
+    env = {**algo_env(algo), "CAIL_NVLS_UNIT": "65536"}
+    exact = ["--tol", "1e-4"] if algo == "nvls" else ["--bits"]
+    for np in nranks():
+        r = mpirun(np, ["cail_check", "-m", "slots", "-d"] + exact, preload="cuda", env=env, timeout=900)
+        assert ok(r), f"np={np} algo={algo}\n" + r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.multigpu
 def test_registration_cache_stress():
     need_gpus(2)
     np = nranks()[-1]

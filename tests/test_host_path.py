@@ -45,6 +45,14 @@ def test_edge_cases(np):
     assert ok(r), r.stdout + r.stderr
 
 
+@pytest.mark.parametrize("np", [2, 3])
+def test_large_ragged_and_unaligned_messages_host(np):
+    # the host algorithms on the same ragged / off-boundary cases the NVLink
+    # test runs (2 MiB + 12 bytes of floats here, to keep the CPU run short)
+    r = mpirun(np, ["cail_check", "-m", "slots", "-c", "524291", "--tol", "1e-4"])
+    assert ok(r), r.stdout + r.stderr
+
+
 @pytest.mark.parametrize("algo", ALGOS)
 def test_config1_host_only(algo):
     """Host-only build, np=2: FLOAT SUM 262144 uniform[-1,1) seeded seed+rank and
