@@ -936,11 +936,11 @@ bool stream_ordered_ok(const cail_dev_comm *dc) {
     return cail_global_state.stream_ordered && cail_global_state.stream_sync && dc->done_ev;
 }
 
-int finish_stream_ordered(cail_dev_comm *dc) {
+int finish_stream_ordered(cail_dev_comm *dc, const char *what) {
     if (cudaEventRecord(dc->done_ev, dc->stream) != cudaSuccess ||
         cudaStreamWaitEvent(cudaStreamLegacy, dc->done_ev, 0) != cudaSuccess) {
-        CAIL_ERR("one_shot: ordering the legacy stream after the call failed");
-        return check_status(dc, "one_shot");
+        CAIL_ERR("%s: ordering the legacy stream after the call failed", what);
+        return check_status(dc, what);
     }
     dc->pending = true;
     return MPI_SUCCESS;
@@ -992,7 +992,7 @@ int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
         dc->broken = true;
         return MPI_ERR_OTHER;
     }
-    if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc);
+    if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc, "one_shot");
     return check_status(dc, "one_shot");
 }
 
@@ -1054,7 +1054,7 @@ int run_push(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
         dc->broken = true;
         return MPI_ERR_OTHER;
     }
-    if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc);
+    if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc, "two_shot");
     return check_status(dc, "two_shot");
 }
 
@@ -1380,7 +1380,7 @@ int run_nvls(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t
         dc->broken = true;
         return MPI_ERR_OTHER;
     }
-    if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc);
+    if (allow_ordered && stream_ordered_ok(dc)) return finish_stream_ordered(dc, "nvls");
     return check_status(dc, "nvls");
 }
 
