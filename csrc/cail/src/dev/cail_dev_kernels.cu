@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include "../gpu/cail_ops.h"
+#include "cail_dev_copier.cuh"
 #include "cail_dev_kernels.cuh"
 
 namespace cail {
@@ -43,6 +44,12 @@ __device__ __forceinline__ void st_v4(void *p, uint4 v) {
                  "r"(v.w)
                  : "memory");
 }
+
+// ld_v4 / st_v4 as the copier loop's load/store policy
+struct V4 {
+    static __device__ __forceinline__ uint4 ld(const void *p) { return ld_v4(p); }
+    static __device__ __forceinline__ void st(void *p, uint4 v) { st_v4(p, v); }
+};
 
 template <int OP, typename T>
 __device__ __forceinline__ uint4 vop(uint4 a, uint4 b) {
@@ -608,11 +615,9 @@ __device__ int nvls_check(const NvlsArgs &a) {
     return 0;
 }
 
-// Warp roles of the NVLS kernel: the first kNvlsCopyWarps warps copy units
-// into and out of the CTA's two staging slots, the others run the multimem
-// reduction; thread kNvlsLeader (the first reducer) meets the other ranks.
-constexpr int kNvlsCopyWarps = 4;
-constexpr int kNvlsCopiers = kNvlsCopyWarps * 32;
+// Warp roles of the NVLS kernel (kNvlsCopiers copier threads, see
+// cail_dev_copier.cuh); thread kNvlsLeader (the first reducer) meets the
+// other ranks.
 constexpr int kNvlsReducers = 512 - kNvlsCopiers;
 constexpr int kNvlsLeader = kNvlsCopiers;
 
@@ -642,44 +647,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
     }
 }
 
-// n bytes with the copier threads (tid in [0, kNvlsCopiers)).  Thread tid
-// moves the 16-byte chunks tid, tid + kNvlsCopiers, ... of the unit, the
-// partial last chunk included, whatever the alignment of either end and the
-// unit's length.  The copy-out of a slot and the copy-in that refills it
-// therefore touch every slot byte from the same thread, in program order,
-// and need no barrier between them (a thread that wrote a chunk another
-// thread had not yet copied out would corrupt that unit's result).  Both
-// ends 16-byte aligned: whole chunks as vectors, four in flight per thread;
-// otherwise element by element inside the chunk (an element never straddles
-// two chunks: the slot and the unit's offset are 16-byte multiples).
-template <typename T>
-__device__ __forceinline__ void copier_copy(char *dst, const char *src, size_t n, int tid) {
-    const size_t nv = n / 16;
-    if ((((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
-        constexpr int U = 4;
-        size_t i = tid;
-        for (; i + (U - 1) * kNvlsCopiers < nv; i += U * kNvlsCopiers) {
-            uint4 v[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) v[u] = ld_v4(src + (i + u * kNvlsCopiers) * 16);
-#pragma unroll
-            for (int u = 0; u < U; ++u) st_v4(dst + (i + u * kNvlsCopiers) * 16, v[u]);
-        }
-        for (; i < nv; i += kNvlsCopiers) st_v4(dst + i * 16, ld_v4(src + i * 16));
-    } else {
-        constexpr int E = 16 / (int)sizeof(T);
-        for (size_t i = tid; i < nv; i += kNvlsCopiers) {
-            T v[E];
-#pragma unroll
-            for (int e = 0; e < E; ++e) v[e] = reinterpret_cast<const T *>(src + i * 16)[e];
-#pragma unroll
-            for (int e = 0; e < E; ++e) reinterpret_cast<T *>(dst + i * 16)[e] = v[e];
-        }
-    }
-    if (nv % kNvlsCopiers == (size_t)tid)  // the partial last chunk (none when n is a multiple of 16)
-        for (size_t off = nv * 16; off < n; off += sizeof(T))
-            *reinterpret_cast<T *>(dst + off) = *reinterpret_cast<const T *>(src + off);
-}
 
 // One CTA per staging pair: copier warps move unit k + 1 in and unit k - 1
 // out while the reducer warps run unit k through the switch, so the local
@@ -729,10 +696,10 @@ __global__ void __launch_bounds__(512, 2) nvls_kernel(NvlsArgs a) {
                 const uint32_t j = k - 2;
                 if (!mbar_wait(&done[j & 1], (j >> 1) & 1, globaltimer() + 4 * a.timeout_ns, fail)) return;
                 fence_proxy_alias();
-                copier_copy<T>(a.dst + unit_off(j), slot_uc(j), unit_len(j), tid);
+                copier_copy<T, V4>(a.dst + unit_off(j), slot_uc(j), unit_len(j), tid);
             }
             if (k < K) {  // copy-in of unit k into the slot just emptied
-                copier_copy<T>(slot_uc(k), a.src + unit_off(k), unit_len(k), tid);
+                copier_copy<T, V4>(slot_uc(k), a.src + unit_off(k), unit_len(k), tid);
                 mbar_arrive(&full[k & 1]);
             }
         }

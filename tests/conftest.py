@@ -27,7 +27,7 @@ _built = {"done": False}
 def _stale():
     """True when a native artefact is missing or older than a source file."""
     outs = [os.path.join(LIB, n) for n in ("libmpi.so", "libcail.so", "libcail_host.so")]
-    outs += [os.path.join(BIN, n) for n in ("cail-mpirun", "cail_check", "cail_check_linked")]
+    outs += [os.path.join(BIN, n) for n in ("cail-mpirun", "cail_check", "cail_check_linked", "cail_copier_check")]
     if not all(os.path.exists(p) for p in outs):
         return True
     oldest = min(os.path.getmtime(p) for p in outs)
