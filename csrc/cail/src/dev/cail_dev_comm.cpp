@@ -228,8 +228,8 @@ struct cail_dev_comm {
     int push_gmax = 0;
     size_t push_piece_max = 0, push_area = 0;
     uint32_t push_epoch = 0;
-    // one-shot: largest piece and bytes of its area
-    size_t os_piece_max = 0, os_area = 0;
+    // one-shot: largest piece and bytes of its area; piece of the last call
+    size_t os_piece_max = 0, os_area = 0, os_piece_last = 0;
     DevStatus *status_h = nullptr, *status_d = nullptr;
     // host exchange
     XSlot *xs = nullptr;
@@ -960,6 +960,29 @@ int poll_pending(cail_dev_comm *dc) {
     return MPI_ERR_OTHER;
 }
 
+// A one-shot call whose piece differs from the previous one-shot call's lays
+// its slots out differently (the kernel's slot offsets scale with the
+// piece), so it must not push while a peer still folds the previous call's
+// last rounds.  Every rank waits for its own queued work, then all meet at
+// a host barrier on the exchange segment.  Messages up to push_gmax x 8 KiB
+// all have the 8 KiB piece and never come here.
+int oneshot_relayout(cail_dev_comm *dc) {
+    if (cudaStreamSynchronize(dc->stream) != cudaSuccess) {
+        CAIL_ERR("one_shot: waiting for the previous call failed");
+        dc->broken = true;
+        return MPI_ERR_OTHER;
+    }
+    if (dc->status_h->code != 0) return check_status(dc, "one_shot");  // reports an earlier timeout
+    dc->pending = false;
+    XSlot &me = dc->xs[dc->rank];
+    const uint64_t seq = ++dc->xseq;
+    me.arrive.store(seq, std::memory_order_release);
+    const int rc = host_wait(dc, false, seq);
+    me.depart.store(rc == MPI_SUCCESS ? seq : (seq | kXErr), std::memory_order_release);
+    if (rc != MPI_SUCCESS) dc->broken = true;
+    return rc;
+}
+
 int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, size_t esz, int op, int ec,
                 bool allow_ordered) {
     const size_t bytes = count * esz;
@@ -967,7 +990,13 @@ int run_oneshot(cail_dev_comm *dc, const char *src, char *dst, size_t count, siz
     memset(&a, 0, sizeof(a));
     size_t piece = 0;
     oneshot_shape(bytes, dc->push_gmax, dc->os_piece_max, &piece, &a.G);
+    if (dc->os_piece_last && piece != dc->os_piece_last) {
+        const int rc = oneshot_relayout(dc);
+        if (rc != MPI_SUCCESS) return rc;
+    }
+    dc->os_piece_last = piece;
     a.piece = piece;
+    a.sg = dc->push_gmax;  // the area holds 3 x push_gmax x P x os_piece_max
     a.bytes = bytes;
     a.area = dc->os_area;
     a.P = dc->P;
@@ -1608,14 +1637,16 @@ int cail_dev_plan(int kind, int P, size_t count, size_t esz, int vec, int gmax, 
     if (P < 2 || P > kMaxRanks || gmax < 1 || gmax > cail::kMaxBlocks || !out) return -1;
     const size_t bytes = count * esz;
     if (kind == 0) {
-        if (nout < 3) return -1;
+        if (nout < 5) return -1;
         size_t piece = 0;
         int G = 0;
         oneshot_shape(bytes, gmax, os_piece_max_for(P, gmax), &piece, &G);
         out[0] = (unsigned long long)G;
         out[1] = piece;
         out[2] = os_area_for(P, gmax, os_piece_max_for(P, gmax));
-        return 3;
+        out[3] = (unsigned long long)gmax;  // slot stride in CTAs (run_oneshot: a.sg)
+        out[4] = os_piece_max_for(P, gmax);  // the largest piece the area holds
+        return 5;
     }
     if (kind == 1) {
         if (nout < 5 + P + 1) return -1;
@@ -1675,6 +1706,7 @@ int cail_test_device_timeout(int timeout_ms) {
         a.rounds_done[0] = (uint32_t *)ws + cail::kOsRoundsBase;
         a.bytes = part;
         a.piece = piece;
+        a.sg = 1;
         a.area = area;
         a.P = 2;
         a.rank0 = 0;

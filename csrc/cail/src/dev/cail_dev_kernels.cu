@@ -125,7 +125,7 @@ __device__ int oneshot_check(const OneShotArgs &a) {
         a.rank0 + (int)(gridDim.x / (unsigned)a.G) > a.P)
         return 2;
     if (a.piece == 0 || a.piece % 16) return 3;
-    if ((size_t)kOsSlots * a.G * a.P * a.piece > a.area) return 4;
+    if (a.sg < a.G || (size_t)kOsSlots * a.sg * a.P * a.piece > a.area) return 4;
     if (a.bytes % sizeof(T)) return 5;
     for (int q = 0; q < a.P; ++q)
         if (!a.slots[q] || ((uintptr_t)a.slots[q] & 15) || !a.flags[q]) return 7;
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(512, 2) oneshot_kernel(OneShotArgs a) {
     const uint32_t base = a.rounds_done[me][b];  // read by every thread before thread 0 updates it
     __syncthreads();
     auto off = [&](uint32_t k) { return ((size_t)k * a.G + b) * a.piece; };
-    auto slot_of = [&](uint32_t e, int q) { return (((size_t)(e % kOsSlots) * a.G + b) * P + q) * a.piece; };
+    auto slot_of = [&](uint32_t e, int q) { return (((size_t)(e % kOsSlots) * a.sg + b) * P + q) * a.piece; };
     auto push = [&](uint32_t k) {
         const uint32_t e = base + k + 1;
         const size_t o = off(k);

@@ -48,6 +48,15 @@ struct OneShotArgs {
     size_t bytes;                    // message bytes
     size_t piece;                    // bytes per CTA and round (a multiple of 16)
     size_t area;                     // bytes of each one-shot area
+    // Slot layout: slot s of CTA b for source q starts at
+    // ((s * sg + b) * P + q) * piece, with sg >= G fixed for the
+    // communicator (its largest CTA count).  A CTA's slots then sit at the
+    // same place in every call with the same piece, whatever the call's G:
+    // a rank may start pushing its next call while a peer still folds the
+    // last rounds of the previous one, and the slot rotation protects only
+    // the slots of the same CTA.  (The host separates calls whose pieces
+    // differ; every message up to sg x 8 KiB has the 8 KiB piece.)
+    int sg;
     int P, rank0, G;
     int vec;                         // every user buffer is 16-byte aligned
     unsigned long long timeout_ns;

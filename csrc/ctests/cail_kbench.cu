@@ -61,10 +61,12 @@ struct Emu {
     Bufs b;
     char *ws[cail::kMaxRanks] = {};
     size_t os_area = 0, area = 0;
+    int os_g = 0;
     uint32_t epoch = 0;
     cail::DevStatus *st = nullptr;
     static constexpr size_t kFlags = 64 << 10;
     bool init(int P, int G, size_t piece) {
+        os_g = G;
         os_area = ((size_t)cail::kOsSlots * G * P * piece + 255) / 256 * 256;
         area = ((size_t)2 * G * P * piece + 255) / 256 * 256;
         for (int q = 0; q < P; ++q)
@@ -94,6 +96,7 @@ struct Emu {
         }
         a.rank0 = 0;
         a.area = os_area;
+        a.sg = os_g;  // slot stride: the largest CTA count the area was sized for
         a.timeout_ns = timeout_ns;
         a.status = st;
     }

@@ -198,14 +198,17 @@ def test_nvlink_p2p_matrix_bit_exact(algo):
 
 
 @pytest.mark.multigpu
-@pytest.mark.parametrize("algo", ["auto", "nvls", "two_shot", "two_shot_zerocopy", "ce_two_shot"])
+@pytest.mark.parametrize("algo", ["auto", "nvls", "two_shot", "two_shot_zerocopy", "ce_two_shot", "one_shot"])
 def test_nvlink_config3_coverage(algo):
     """20 datatypes x SUM/PROD/MAX/MIN at counts 1,000,003 and 4,194,304 at
     every available rank count; integers bit-exact, floats within
-    reassociation tolerance (NVLS) or bit-exact (two-shot, both kinds)."""
+    reassociation tolerance (NVLS) or bit-exact (the P2P kernels).  Forced
+    one_shot changes its piece between these sizes and element types, so
+    its host barrier before a new slot layout runs many times."""
     need_gpus(2)
     for np in nranks():
-        args = ["cail_check", "-m", "config3", "-d"] + (["--bits"] if "two_shot" in algo else ["--tol", "1e-4"])
+        exact = "two_shot" in algo or algo == "one_shot"
+        args = ["cail_check", "-m", "config3", "-d"] + (["--bits"] if exact else ["--tol", "1e-4"])
         r = mpirun(np, args, preload="cuda", env=algo_env(algo), timeout=1200)
         assert ok(r), f"np={np} algo={algo}\n" + r.stdout[-3000:] + r.stderr[-3000:]
 

@@ -10,8 +10,9 @@ whole message:
   units in the vector path (and on elements otherwise), only the last slice
   holds the ragged tail, rounds x CTAs x piece covers the longest slice, and
   the slots of all CTAs fit the workspace area;
-* one-shot: CTAs x rounds x piece covers the message and three slots per
-  CTA and rank fit the area;
+* one-shot: CTAs x rounds x piece covers the message, three slots per CTA
+  and rank fit the area, and the slot layout depends on the call only
+  through its piece (8 KiB for every message up to gmax x 8 KiB);
 * NVLS: every CTA gets the same number of units, all units are covered,
   no CTA is idle, and the two slots per CTA fit the staging area.
 """
@@ -67,16 +68,30 @@ def test_push_two_shot_shapes(lib, P, gmax):
 @pytest.mark.parametrize("P", [2, 3, 4, 8])
 @pytest.mark.parametrize("gmax", [296, 148])
 def test_one_shot_shapes(lib, P, gmax):
+    layouts = set()
     for esz in (1, 4, 8):
         for elems in SIZES:
-            G, piece, area = plan(lib, 0, P, elems, esz, 1, gmax)
+            G, piece, area, sg, piece_max = plan(lib, 0, P, elems, esz, 1, gmax)
             nbytes = elems * esz
-            assert 1 <= G <= gmax and piece % 16 == 0 and piece >= 8192
-            assert 3 * G * P * piece <= area  # three rotating slots per CTA and source
+            assert 1 <= G <= gmax and piece % 16 == 0 and 8192 <= piece <= piece_max
+            # slot s of CTA b for source q at ((s * sg + b) * P + q) * piece:
+            # the CTA stride is the communicator's, three rotating slots per
+            # CTA and source fit the area
+            assert sg == gmax and sg >= G
+            assert 3 * sg * P * piece <= area
+            if nbytes <= gmax * 8192:
+                assert piece == 8192  # one layout for every message up to gmax x 8 KiB
+            layouts.add((sg, piece, area))
             # CTA b handles offsets (k*G + b)*piece: every byte is covered
             rounds = -(-nbytes // (G * piece))
             assert rounds * G * piece >= nbytes
             assert G == 1 or (G - 1) * piece < nbytes  # no CTA without a piece
+    # the layout depends on the call only through its piece (the host puts a
+    # barrier between calls whose pieces differ): a CTA's slots sit at the
+    # same place in every call of one piece, so a peer still folding the
+    # previous call's last rounds never sees this call's pushes land in the
+    # slots it reads
+    assert len({(sg, area) for sg, _, area in layouts}) == 1
 
 
 @pytest.mark.parametrize("gmax", [296, 148])
