@@ -578,29 +578,6 @@ __device__ __forceinline__ bool nvls_meet(const NvlsArgs &a, size_t ctr, uint32_
     return true;
 }
 
-// n bytes between this GPU's buffers with the CTA's threads; 16-byte
-// vectors (four in flight per thread) when both ends are aligned.
-template <typename T>
-__device__ __forceinline__ void cta_copy(char *dst, const char *src, size_t n) {
-    size_t done = 0;
-    if ((((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
-        constexpr int U = 4;
-        const size_t nv = n / 16;
-        size_t i = threadIdx.x;
-        for (; i + (U - 1) * blockDim.x < nv; i += U * blockDim.x) {
-            uint4 v[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) v[u] = ld_v4(src + (i + u * blockDim.x) * 16);
-#pragma unroll
-            for (int u = 0; u < U; ++u) st_v4(dst + (i + u * blockDim.x) * 16, v[u]);
-        }
-        for (; i < nv; i += blockDim.x) st_v4(dst + i * 16, ld_v4(src + i * 16));
-        done = nv * 16;
-    }
-    for (size_t e = done / sizeof(T) + threadIdx.x; e < n / sizeof(T); e += blockDim.x)
-        reinterpret_cast<T *>(dst)[e] = reinterpret_cast<const T *>(src)[e];
-}
-
 // CAIL_DEVICE_CHECKS for the NVLS kernel: 0 when the arguments are
 // consistent, else the number of the failed check.
 template <typename T, int MB>
