@@ -814,7 +814,11 @@ cail_dev_comm *create_context(MPI_Comm comm) {
         if (o < 0 || cudaDeviceCanAccessPeer(&can, dc->dev, o) != cudaSuccess || !can) ok = false;
     }
     if (dc->shared_gpu) all_nvls = false;
+    // Launch shapes and workspace layouts derive from the SM count and must
+    // be the same on every rank: take the smallest over the ranks.
     dc->sms = me.sms > 0 ? me.sms : 148;
+    for (int q = 0; ok && q < dc->P; ++q)
+        if (all[q].sms > 0 && all[q].sms < dc->sms) dc->sms = all[q].sms;
     if (!agree(comm, ok)) {
         CAIL_DBG("nvlink path unavailable on this communicator (probe)");
         return dc;  // ok == false
