@@ -107,3 +107,52 @@ def test_nvls_shapes(lib, gmax):
         assert 2 * blocks * unit <= staging
     # 1 GiB of 1 MiB units on 296 CTAs: 256 CTAs of exactly 4 units
     assert plan(lib, 2, 8, 1 << 28, 4, 1, 296)[:2] == [256, 1 << 20]
+
+
+def _os_slot_block(s, b, sg, P, piece):
+    """Bytes of slot s of CTA b for all P sources: [start, end).  This is the
+    one-shot kernel's slot_of(e, q) = ((e % 3 * sg + b) * P + q) * piece
+    (oneshot_kernel in cail_dev_kernels.cu) taken over q = 0 .. P-1."""
+    start = (s * sg + b) * P * piece
+    return start, start + P * piece
+
+
+@pytest.mark.parametrize("P", [2, 4, 8])
+def test_one_shot_next_call_never_writes_slots_a_peer_may_still_fold(lib, P):
+    """A rank starts pushing its next one-shot call as soon as its own kernel
+    has finished, while a peer may still fold the last two rounds of every
+    CTA of the previous call.  Over random sequences of message sizes (with
+    the per-CTA round counters the kernel keeps), the first pushes of each
+    call must land outside every slot the previous call may still read,
+    unless the piece changed, in which case the host barrier separates the
+    calls."""
+    import random
+
+    gmax = 296
+    rng = random.Random(P)
+    sizes = [1 << k for k in range(10, 25)] + [3000, 100003, 777777, 5 << 20]
+    count = [0] * gmax  # completed rounds per CTA, the same on every rank
+    prev = None  # (piece, {cta: [slots it may still fold]}, sg)
+    checked = 0
+    for _ in range(400):
+        nbytes = rng.choice(sizes)
+        G, piece, area, sg, _ = plan(lib, 0, P, nbytes, 1, 1, gmax)
+        rounds = [len(range(b * piece, nbytes, G * piece)) for b in range(G)]
+        if prev is not None and prev[0] == piece:
+            busy = [_os_slot_block(s, b, prev[2], P, piece) for b, ss in prev[1].items() for s in ss]
+            for b in range(G):
+                if rounds[b] == 0:
+                    continue
+                lo, hi = _os_slot_block((count[b] + 1) % 3, b, sg, P, piece)  # round 0 of this call
+                assert hi <= area
+                for blo, bhi in busy:
+                    assert hi <= blo or bhi <= lo, (nbytes, b, (lo, hi), (blo, bhi))
+                    checked += 1
+        last = {}
+        for b in range(G):
+            if rounds[b]:
+                epochs = [count[b] + rounds[b] - i for i in range(min(2, rounds[b]))]  # last two rounds
+                last[b] = [e % 3 for e in epochs]
+                count[b] += rounds[b]
+        prev = (piece, last, sg)
+    assert checked > 1000
