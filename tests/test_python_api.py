@@ -31,6 +31,27 @@ def test_dtype_mapping():
         mpi_datatype(torch.bfloat16)
 
 
+def test_tensor_api_rejects_bad_arguments_before_any_mpi_call():
+    """Argument errors surface as Python exceptions before MPI is touched
+    (no cail_b200.init() here): non-contiguous tensors, size or dtype
+    mismatches, counts that do not fit MPI's int, and unknown operators."""
+    from cail_b200.ops import allreduce, allreduce_, mpi_op
+
+    with pytest.raises(ValueError, match="contiguous"):
+        allreduce_(torch.zeros(4, 4).t())
+    with pytest.raises(ValueError):
+        allreduce(torch.zeros(4), torch.zeros(5))
+    with pytest.raises(ValueError):
+        allreduce(torch.zeros(8)[::2], torch.zeros(4))
+    with pytest.raises(TypeError, match="dtypes differ"):
+        allreduce(torch.zeros(4), torch.zeros(4, dtype=torch.float64))
+    big = torch.empty(2**31, dtype=torch.int8, device="meta")  # 2^31 elements, nothing allocated
+    with pytest.raises(ValueError, match="int"):
+        allreduce_(big)
+    with pytest.raises(KeyError):
+        mpi_op("xor")
+
+
 def test_stream_ordered_toggle_returns_previous_mode():
     code = ("import ctypes; ctypes.CDLL('build/lib/libmpi.so', mode=ctypes.RTLD_GLOBAL); "
             "c = ctypes.CDLL('build/lib/libcail.so'); "
