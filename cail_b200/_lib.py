@@ -63,7 +63,7 @@ _loaded: Optional[Libs] = None
 
 
 def _setup(lib: ctypes.CDLL) -> None:
-    vp, i, u64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64
+    vp, i = ctypes.c_void_p, ctypes.c_int
     for name, args in {
         "MPI_Allreduce": [vp, vp, i, i, i, i],
         "MPI_Init_thread": [vp, vp, i, ctypes.POINTER(i)],
@@ -83,7 +83,6 @@ def _setup(lib: ctypes.CDLL) -> None:
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = ctypes.c_int
-    _ = u64
 
 
 def load(impl: str = "ours", host: bool = False) -> Libs:
