@@ -624,7 +624,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
     }
 }
 
-
 // One CTA per staging pair: copier warps move unit k + 1 in and unit k - 1
 // out while the reducer warps run unit k through the switch, so the local
 // copies overlap the NVLink traffic.  Slot k % 2 holds unit k; the copiers
