@@ -970,6 +970,8 @@ int poll_pending(cail_dev_comm *dc) {
 // last rounds.  Every rank waits for its own queued work, then all meet at
 // a host barrier on the exchange segment.  Messages up to push_gmax x 8 KiB
 // all have the 8 KiB piece and never come here.
+bool peer_failed(const cail_dev_comm *dc, bool depart);
+
 int oneshot_relayout(cail_dev_comm *dc) {
     if (cudaStreamSynchronize(dc->stream) != cudaSuccess) {
         CAIL_ERR("one_shot: waiting for the previous call failed");
@@ -981,7 +983,12 @@ int oneshot_relayout(cail_dev_comm *dc) {
     XSlot &me = dc->xs[dc->rank];
     const uint64_t seq = ++dc->xseq;
     me.arrive.store(seq, std::memory_order_release);
-    const int rc = host_wait(dc, false, seq);
+    int rc = host_wait(dc, false, seq);
+    if (rc == MPI_SUCCESS && peer_failed(dc, false)) {
+        // a peer gave up at this barrier: nobody may launch into its slots
+        CAIL_ERR("one_shot: a peer failed at the barrier before a new slot layout; not launching");
+        rc = MPI_ERR_OTHER;
+    }
     me.depart.store(rc == MPI_SUCCESS ? seq : (seq | kXErr), std::memory_order_release);
     if (rc != MPI_SUCCESS) dc->broken = true;
     return rc;
