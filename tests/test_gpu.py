@@ -178,15 +178,19 @@ def nranks():
 
 
 def algo_env(algo):
-    """CAIL_ALGO for a test parameter; two_shot_zerocopy is two_shot over the
-    user buffers (CAIL_TWOSHOT_ZEROCOPY=1) instead of the push kernel."""
+    """CAIL_ALGO for a test parameter.  Blocking two_shot calls run the
+    zero-copy kernel by default: two_shot_zerocopy forces it
+    (CAIL_TWOSHOT_ZEROCOPY=1) and two_shot_push forces the push kernel
+    over the workspace (CAIL_TWOSHOT_ZEROCOPY=0)."""
     if algo == "two_shot_zerocopy":
         return {"CAIL_ALGO": "two_shot", "CAIL_TWOSHOT_ZEROCOPY": "1"}
+    if algo == "two_shot_push":
+        return {"CAIL_ALGO": "two_shot", "CAIL_TWOSHOT_ZEROCOPY": "0"}
     return {"CAIL_ALGO": algo}
 
 
 @pytest.mark.multigpu
-@pytest.mark.parametrize("algo", ["one_shot", "two_shot", "two_shot_zerocopy", "ce_two_shot"])
+@pytest.mark.parametrize("algo", ["one_shot", "two_shot_push", "two_shot_zerocopy", "ce_two_shot"])
 def test_nvlink_p2p_matrix_bit_exact(algo):
     # counts {1,2,3,4099,4100,4102}: heads, tails, fewer elements than ranks;
     # separate and in place; floats bit-identical to the rank-order oracle
@@ -198,7 +202,7 @@ def test_nvlink_p2p_matrix_bit_exact(algo):
 
 
 @pytest.mark.multigpu
-@pytest.mark.parametrize("algo", ["auto", "nvls", "two_shot", "two_shot_zerocopy", "ce_two_shot", "one_shot"])
+@pytest.mark.parametrize("algo", ["auto", "nvls", "two_shot_push", "two_shot_zerocopy", "ce_two_shot", "one_shot"])
 def test_nvlink_config3_coverage(algo):
     """20 datatypes x SUM/PROD/MAX/MIN at counts 1,000,003 and 4,194,304 at
     every available rank count; integers bit-exact, floats within
@@ -224,7 +228,7 @@ def test_nvlink_edge_and_config1():
 
 
 @pytest.mark.multigpu
-@pytest.mark.parametrize("algo", ["nvls", "two_shot", "two_shot_zerocopy", "one_shot"])
+@pytest.mark.parametrize("algo", ["nvls", "two_shot_push", "two_shot_zerocopy", "one_shot"])
 def test_large_ragged_and_unaligned_messages(algo):
     """Messages of 40 MiB plus a few bytes (not a multiple of 16 bytes), on
     buffers one or three elements off a 16-byte boundary, separate and in
