@@ -213,6 +213,25 @@ def test_stats_dump():
     assert m and int(m.group(3)) == 4 and int(m.group(2)) >= 1
 
 
+def test_scratch_cache_only_grows():
+    """The point-to-point algorithms' scratch buffer is reallocated only when
+    a request exceeds it and is otherwise reused (the reference's grow-only
+    cache, src/core/cail_buf.c:28-69): over the matrix's rising and falling
+    sizes, the allocations each rank logs only grow, and every reuse serves
+    a request no larger than the cached size."""
+    r = mpirun(2, ["cail_check", "-m", "matrix", "-c", "1000"],
+               env={"CAIL_DEBUG": "1", "CAIL_ALGO": "recursive_doubling", "CAIL_MIN_MSG_SIZE": "0"})
+    assert ok(r), r.stdout + r.stderr
+    allocs = [int(n) for n in re.findall(r"buf: allocated (\d+) bytes", r.stderr)]
+    reuses = [(int(c), int(q)) for c, q in re.findall(r"buf: reusing cached (\d+) bytes \(requested (\d+)\)", r.stderr)]
+    assert allocs and reuses
+    # both ranks log the same rising sequence, interleaved: never a decrease
+    assert all(a <= b for a, b in zip(allocs, allocs[1:])), allocs
+    assert len(allocs) <= 2 * len(set(allocs))
+    assert all(q <= c for c, q in reuses)
+    assert len(reuses) > len(allocs)
+
+
 def test_trace_file(tmp_path):
     path = tmp_path / "trace.csv"
     r = mpirun(2, ["cail_check", "-m", "config1"], env={"CAIL_TRACE": str(path), "CAIL_ALGO": "rabenseifner"})
