@@ -52,6 +52,41 @@ def test_tensor_api_rejects_bad_arguments_before_any_mpi_call():
         mpi_op("xor")
 
 
+def test_handle_table_maps_23_datatypes_to_12_types_and_4_ops():
+    """The interposer accepts the 20 documented datatypes plus the aliases
+    MPI_SIGNED_CHAR, MPI_BYTE and MPI_LONG_LONG_INT, mapped onto 12 element
+    types with the reference's enum values (src/core/cail_types.c:5-40);
+    anything else, and operators other than SUM/PROD/MAX/MIN, is
+    unsupported (-1) and passes through to PMPI."""
+    import ctypes
+
+    from conftest import LIB, ensure_build
+    from cail_b200 import _lib
+
+    ensure_build()
+    ctypes.CDLL(os.path.join(LIB, "libmpi.so"), mode=ctypes.RTLD_GLOBAL)
+    c = ctypes.CDLL(os.path.join(LIB, "libcail_host.so"))
+    H = _lib.H
+    want = {  # handle -> (cail element type, bytes)
+        "MPI_CHAR": (0, 1), "MPI_SIGNED_CHAR": (0, 1), "MPI_INT8_T": (0, 1),
+        "MPI_UNSIGNED_CHAR": (6, 1), "MPI_BYTE": (6, 1), "MPI_UINT8_T": (6, 1),
+        "MPI_SHORT": (10, 2), "MPI_INT16_T": (10, 2), "MPI_UNSIGNED_SHORT": (11, 2), "MPI_UINT16_T": (11, 2),
+        "MPI_INT": (1, 4), "MPI_INT32_T": (1, 4), "MPI_UNSIGNED": (7, 4), "MPI_UINT32_T": (7, 4),
+        "MPI_LONG": (2, 8), "MPI_UNSIGNED_LONG": (8, 8),
+        "MPI_LONG_LONG": (5, 8), "MPI_LONG_LONG_INT": (5, 8), "MPI_INT64_T": (5, 8),
+        "MPI_UNSIGNED_LONG_LONG": (9, 8), "MPI_UINT64_T": (9, 8),
+        "MPI_FLOAT": (3, 4), "MPI_DOUBLE": (4, 8),
+    }
+    assert len(want) == 23
+    for name, (dt, size) in want.items():
+        assert c.cail_mpi_type_to_dtype(H[name]) == dt, name
+        assert c.cail_type_size(dt) == size, name
+    assert len({dt for dt, _ in want.values()}) == 12
+    assert c.cail_mpi_type_to_dtype(H["MPI_LONG_DOUBLE"]) == -1
+    for name, op in (("MPI_SUM", 0), ("MPI_PROD", 1), ("MPI_MAX", 2), ("MPI_MIN", 3), ("MPI_BAND", -1)):
+        assert c.cail_mpi_op_to_optype(H[name]) == op, name
+
+
 def test_stream_ordered_toggle_returns_previous_mode():
     code = ("import ctypes; ctypes.CDLL('build/lib/libmpi.so', mode=ctypes.RTLD_GLOBAL); "
             "c = ctypes.CDLL('build/lib/libcail.so'); "
