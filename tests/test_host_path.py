@@ -213,6 +213,18 @@ def test_stats_dump():
     assert m and int(m.group(3)) == 4 and int(m.group(2)) >= 1
 
 
+@pytest.mark.parametrize("algo", ["recursive_doubling", "ring", "rabenseifner"])
+def test_dispatch_error_falls_back_to_pmpi(algo):
+    """An algorithm that fails (here its scratch request, injected with
+    CAIL_FI_SCRATCH_FAIL=1) makes the shim retry through PMPI_Allreduce
+    (the reference's cail_pmpi.c:73-77): every result still matches PMPI."""
+    r = mpirun(2, ["cail_check", "-m", "basic"],
+               env={"CAIL_FI_SCRATCH_FAIL": "1", "CAIL_ALGO": algo, "CAIL_MIN_MSG_SIZE": "0", "CAIL_DEBUG": "1"})
+    assert ok(r), r.stdout + r.stderr
+    assert "injected by CAIL_FI_SCRATCH_FAIL" in r.stderr
+    assert "falling back to PMPI" in r.stderr
+
+
 def test_scratch_cache_only_grows():
     """The point-to-point algorithms' scratch buffer is reallocated only when
     a request exceeds it and is otherwise reused (the reference's grow-only
