@@ -3,8 +3,9 @@
 The reference (cornelisnetworks/cail) is a C/CUDA library built with
 autotools; it has no Python packaging, so `pip install` of it fails with
 "Neither 'setup.py' nor 'pyproject.toml' found", and autoreconf is not
-available here.  This script copies its sources (read-only tree, default
-/root/reference, or $CAIL_REFERENCE_SRC) to baseline/_ref/src without
+available here.  This script copies its sources (a read-only checkout: --src,
+else $CAIL_REFERENCE_SRC, else a `reference` directory beside this
+repository) to baseline/_ref/src without
 changing a byte, and compiles them the way its configure script would with
 
     --with-cuda --with-cuda-arch=sm_100a     -> baseline/_ref/lib/libcail.so
@@ -85,7 +86,8 @@ def build(src_root: str) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     # this script is the one place that reads the reference checkout
-    ap.add_argument("--src", default=os.environ.get("CAIL_REFERENCE_SRC", "/root/reference"))
+    sibling = os.path.normpath(os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "reference"))
+    ap.add_argument("--src", default=os.environ.get("CAIL_REFERENCE_SRC", sibling))
     ap.add_argument("--if-present", action="store_true",
                     help="exit quietly when the reference sources are not there")
     a = ap.parse_args()
